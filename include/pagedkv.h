@@ -1,0 +1,202 @@
+/*
+ * pagedkv.h - C ABI of the B200 paged KV-cache hot path.
+ *
+ * This is the drop-in boundary that replaces the Python hot path of
+ * PagedCore (src/pagedcore/kv_cache.py and src/pagedcore/attention.py).
+ * Every entry point takes plain pointers and sizes; no framework types
+ * cross this boundary.  Device pointers are CUDA device addresses on the
+ * current device; `stream` is a cudaStream_t passed as void*.
+ *
+ * Status convention: every int-returning function returns PKV_OK (0) on
+ * success, otherwise one of the PKV_* codes below, and the calling thread's
+ * message is available from pkv_last_error().  A host binding maps
+ * PKV_VALUE_ERROR -> ValueError, PKV_RUNTIME_ERROR / PKV_CUDA_ERROR ->
+ * RuntimeError, PKV_KEY_ERROR -> KeyError, which is the exception contract of
+ * the reference's KVAllocator and paged_attention.  A failing call leaves
+ * the ledger unchanged (kv_cache.py:174-178, 204-219).
+ *
+ * Pool layout (kv_cache.py:39-43): FP16 [22][2][num_blocks][16][4][64],
+ * contiguous.  A slot id is physical_block * 16 + slot_in_block.
+ */
+#ifndef PAGEDKV_H
+#define PAGEDKV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PKV_ABI_VERSION 1
+
+/* Geometry fixed by the reference (kv_cache.py:39-43, 72-82; config.py:24-89). */
+#define PKV_LAYERS 22
+#define PKV_KV_HEADS 4
+#define PKV_QUERY_HEADS 32
+#define PKV_HEAD_DIM 64
+#define PKV_BLOCK_TOKENS 16
+#define PKV_CONTEXT_LIMIT 2048
+#define PKV_MAX_CREDITS 128
+
+enum {
+    PKV_OK = 0,
+    PKV_VALUE_ERROR = 1,
+    PKV_RUNTIME_ERROR = 2,
+    PKV_KEY_ERROR = 3,
+    PKV_CUDA_ERROR = 4
+};
+
+/* Validation levels of a ledger. FULL re-checks every invariant of
+ * KVAllocator._assert_accounting (kv_cache.py:314-357) on every call;
+ * INCREMENTAL checks only the requests and blocks a call touches. */
+enum { PKV_VALIDATE_INCREMENTAL = 0, PKV_VALIDATE_FULL = 1 };
+
+/* Device error-flag bits set by the kernels (host reads the int32 flag). */
+enum {
+    PKV_DEVICE_BAD_BLOCK = 1,     /* physical block id outside [0, num_blocks) */
+    PKV_DEVICE_BAD_POSITION = 2,  /* RoPE position outside [0, 2048) */
+    PKV_DEVICE_WAIT_TIMEOUT = 4   /* a bounded mbarrier wait gave up */
+};
+
+/* Thread-local message of the last failing call on this thread. */
+const char *pkv_last_error(void);
+int pkv_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Block ledger (host).  Replaces KVAllocator's bookkeeping.                 */
+/* ------------------------------------------------------------------------ */
+typedef struct pkv_ledger pkv_ledger;
+
+/* KVAllocator.__init__ (kv_cache.py:71-90): LIFO free list [N-1, ..., 0],
+ * so the first pops are 0, 1, 2, ... */
+int pkv_ledger_new(int32_t num_blocks, int32_t validation, pkv_ledger **out);
+void pkv_ledger_free(pkv_ledger *ledger);
+int pkv_ledger_set_validation(pkv_ledger *ledger, int32_t validation);
+
+/* KVAllocator.create (kv_cache.py:92-110): grant credits, assign nothing. */
+int pkv_ledger_reserve(pkv_ledger *ledger, int64_t request, int64_t credits);
+
+/* KVAllocator.release_all (kv_cache.py:286-298): the request's first block
+ * becomes the top of the free stack. */
+int pkv_ledger_release(pkv_ledger *ledger, int64_t request);
+
+/* KVAllocator.capacity (kv_cache.py:112-115, 348-357): out = {total, free,
+ * owned, reserved, active_slots, live_cached_token_slots}. */
+int pkv_ledger_capacity(pkv_ledger *ledger, int64_t out[6]);
+
+/* KVAllocator.cached_length / block_table (kv_cache.py:117-125). */
+int pkv_ledger_length(pkv_ledger *ledger, int64_t request, int32_t *out_length);
+int pkv_ledger_table(pkv_ledger *ledger, int64_t request, int32_t *out_blocks,
+                     int32_t capacity, int32_t *out_count);
+
+/* KVAllocator.append, split in two (kv_cache.py:127-179).  plan validates and
+ * writes the slot id of each of `tokens` new positions (new blocks come from
+ * the top of the free stack: free[-1], free[-2], ...) without changing state;
+ * commit publishes them after the device write was issued. */
+int pkv_ledger_append_plan(pkv_ledger *ledger, int64_t request, int32_t tokens,
+                           int32_t *out_slots, int32_t *out_start_position);
+int pkv_ledger_append_commit(pkv_ledger *ledger, int64_t request, int32_t tokens);
+
+/* KVAllocator.append_decode (kv_cache.py:181-219): stage length+1 for each
+ * request, borrowing free[-1], free[-2], ... in request order for requests
+ * whose length is a multiple of 16.  Writes each row's slot id and RoPE
+ * position (= cached length before the append). */
+int pkv_ledger_decode_begin(pkv_ledger *ledger, const int64_t *requests, int32_t count,
+                            int32_t *out_slots, int32_t *out_positions);
+/* write_decode_layer's checks (kv_cache.py:226-243) for one staged request,
+ * or for every staged request when request == -1; returns its slot/position. */
+int pkv_ledger_decode_check(pkv_ledger *ledger, int64_t request, int32_t layer,
+                            int32_t *out_slot, int32_t *out_position);
+/* Record that `layer` was written (kv_cache.py:246); request == -1: all rows. */
+int pkv_ledger_decode_mark(pkv_ledger *ledger, int64_t request, int32_t layer);
+/* Commit needs all 22 layers written (kv_cache.py:208-217); both commit and
+ * abort leave no staged state behind. */
+int pkv_ledger_decode_commit(pkv_ledger *ledger);
+void pkv_ledger_decode_abort(pkv_ledger *ledger);
+int pkv_ledger_decode_active(pkv_ledger *ledger);
+
+/* The table and length that attention sees for one request at `layer`: the
+ * staged view for a staged request whose layer was written, else the
+ * committed one (kv_cache.py:248-270). */
+int pkv_ledger_view(pkv_ledger *ledger, int64_t request, int32_t layer, int32_t *out_blocks,
+                    int32_t capacity, int32_t *out_count, int32_t *out_length);
+
+/* Device-ready metadata for a batch at `layer` (the batched form of
+ * iter_layer_blocks): lengths[count], prefix[count+1] (cumulative block
+ * counts) and the flat concatenation of the tables, flat[prefix[b] + j] =
+ * physical block of logical block j of row b.  flat_capacity bounds flat. */
+int pkv_ledger_batch(pkv_ledger *ledger, const int64_t *requests, int32_t count, int32_t layer,
+                     int32_t *out_lengths, int32_t *out_prefix, int32_t *out_flat,
+                     int32_t flat_capacity, int32_t *out_total_blocks);
+
+/* Full invariant check of kv_cache.py:314-357. */
+int pkv_ledger_audit(pkv_ledger *ledger);
+
+/* Free stack, bottom to top (the reference's _free_blocks list order). */
+int pkv_ledger_free_list(pkv_ledger *ledger, int32_t *out, int32_t capacity, int32_t *out_count);
+/* Replace the free stack by a permutation of itself (seeded fragmentation;
+ * the reference's invariants treat the free list as a set, kv_cache.py:331-340). */
+int pkv_ledger_reorder_free(pkv_ledger *ledger, const int32_t *blocks, int32_t count);
+
+/* White-box hooks for corruption tests (the reference's tests write
+ * _sequences and _free_blocks directly, tests/unit/test_kv_cache.py:572-677).
+ * They bypass every check and are never used by the product path. */
+int pkv_ledger_debug_set_table(pkv_ledger *ledger, int64_t request, const int32_t *blocks,
+                               int32_t count, int32_t length);
+int pkv_ledger_debug_set_free(pkv_ledger *ledger, const int32_t *blocks, int32_t count);
+
+/* ------------------------------------------------------------------------ */
+/* Device kernels (sm_100a).                                                */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of the RoPE table the caller provides: FP16 cos[2048][32] followed by
+ * FP16 sin[2048][32], built with the reference's exact op sequence
+ * (dense.py:48-54) so the rotation is bit-exact. */
+int64_t pkv_rope_table_bytes(void);
+
+/* Scatter K/V rows into the pool through slot ids, optionally rotating K
+ * (and a query tensor) with the RoPE table.  Replaces the per-block copy_ of
+ * KVAllocator.append (kv_cache.py:161-172), the two copy_ of
+ * write_decode_layer (kv_cache.py:244-245) and, when rope_table is not NULL,
+ * apply_rope (dense.py:33-61) on K and Q:
+ *   k' = fp16(fp16(k*cos) + fp16(rotate_half(k)*sin)).
+ * key/value: FP16, element (l, t, h, d) at base + l*src_layer_stride +
+ * t*src_token_stride + h*64 + d, for l in [0, layer_count), t in [0, tokens).
+ * Pool layer = layer_begin + l.  slots[t], positions[t]: int32 device arrays.
+ * query_in/query_out (nullable, both or neither): FP16, element (l, t, h, d) at
+ * base + l*q_layer_stride + t*q_token_stride + h*64 + d, h in [0, 32).
+ * All element strides must be multiples of 8 and base pointers 16-byte aligned. */
+int pkv_append_kv(void *pool, int32_t num_blocks, int32_t layer_begin, int32_t layer_count,
+                  const void *key, const void *value, int64_t src_layer_stride,
+                  int64_t src_token_stride, const int32_t *slots, const int32_t *positions,
+                  int32_t tokens, const void *rope_table, const void *query_in, void *query_out,
+                  int64_t q_layer_stride, int64_t q_token_stride, int32_t *error_flag,
+                  void *stream);
+
+/* Launch plan of the split-K decode attention for `total_blocks` 16-token
+ * blocks of a batch of `batch` sequences on `device`: grid size, blocks per
+ * CTA, and the bytes of split partials the caller must provide as workspace. */
+int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
+                    int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes);
+
+/* Batched one-token block-table decode attention with GQA (8 query heads per
+ * KV head).  Replaces paged_attention (attention.py:14-53) for a whole batch:
+ *   out[b,h] = sum_t softmax_t(q[b,h] . K[t, h/8] * 0.125) V[t, h/8]
+ * over the lengths[b] cached tokens of row b at pool layer `layer`, FP32
+ * accumulation, one FP16 rounding.  query: FP16 [batch][32][64] with row
+ * stride query_stride (elements); out likewise with out_stride.
+ * lengths[batch], prefix[batch+1], flat[total_blocks]: int32 device arrays
+ * as written by pkv_ledger_batch.  grid / blocks_per_cta / workspace come from
+ * pkv_decode_plan for the same (batch, total_blocks).  Two launches: the
+ * split kernel and, when some row is split across CTAs, the combine kernel. */
+int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                         int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
+                         const int32_t *flat, int32_t batch, int32_t total_blocks, int32_t grid,
+                         int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
+                         int64_t workspace_bytes, int32_t *error_flag, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDKV_H */

@@ -1,0 +1,556 @@
+// Batched one-token block-table decode attention with GQA on sm_100a.
+//
+// Replaces PagedCore's paged_attention (src/pagedcore/attention.py:14-53),
+// which for one request and one layer computes, in FP32 from FP16 pages,
+//   o[h] = sum_t softmax_t(q[h] . k[t, h/8] * 0.125) v[t, h/8]
+// and rounds once to FP16.  Here a whole batch of requests is served by two
+// launches:
+//
+// 1. decode_attention_kernel - balanced split-K over the batch's 16-token
+//    blocks.  The batch's block tables are concatenated into one flat list
+//    (flat[prefix[b] + j] = physical block of logical block j of row b); CTA
+//    g owns the contiguous global block range [g*W, (g+1)*W), which may cover
+//    the tail of one row, whole short rows and the head of another.  Every
+//    CTA therefore streams the same number of KV bytes whatever the ragged
+//    lengths.  Warp w of a CTA serves KV head w and its 8 query heads (GQA).
+//    Each warp runs its own TMA pipeline: per block, two 2 KiB boxes (the 16
+//    K rows and 16 V rows of its head, 128 B each) land in shared memory with
+//    the 128-byte swizzle, so ldmatrix reads are bank-conflict free.
+//    Tensor-core tiles (mma.sync m16n8k16, FP16 in, FP32 accumulate):
+//      S^T[16 tok x 8 heads] = K[16 x 64] . Q^T[64 x 8]        (4 MMAs)
+//      O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]     (4 MMAs)
+//    so the 8-head GQA group fills the N=8 side exactly.  The S^T accumulator
+//    becomes the P^T operand with two movmatrix transposes.  Softmax is the
+//    online (running max) form in base 2 with FP32 state.  P is rounded to
+//    FP16 for the PV MMA after scaling by 2^15 (p = 2^(s - m + 15) <= 2^15),
+//    which keeps weights down to ~2^-24 of the row maximum representable as
+//    normal FP16 numbers; the normaliser l sums the same rounded weights.
+//    A row fully inside one CTA is normalised and written as FP16 directly;
+//    a row split across CTAs leaves (m, l, O) partials in the workspace at
+//    index row + cta (unique: along the CTA order the (row, cta) pairs form a
+//    monotone staircase, so row + cta strictly increases).
+// 2. decode_combine_kernel - merges the partials of split rows.
+//
+// The pass is HBM-bound: per (row, layer) it reads 1024*L bytes of K/V.
+// Unwritten slots of a row's last block may hold anything (the reference
+// pool is uninitialised, tests fill it with NaN): their scores are masked to
+// -inf and their V rows are zeroed in shared memory before the PV MMA.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdlib>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "pagedkv.h"
+#include "ptx.cuh"
+#include "status.h"
+
+namespace {
+
+constexpr int kHeadDim = PKV_HEAD_DIM;
+constexpr int kKvHeads = PKV_KV_HEADS;
+constexpr int kQueryHeads = PKV_QUERY_HEADS;
+constexpr int kGroup = kQueryHeads / kKvHeads;  // 8 query heads per KV head
+constexpr int kBlockTokens = PKV_BLOCK_TOKENS;
+constexpr int kRowBytes = kHeadDim * 2;                  // 128 B: one head of one token
+constexpr int kTileBytes = kBlockTokens * kRowBytes;     // 2 KiB: one head of one block
+constexpr int kStageBytes = 2 * kTileBytes;              // K tile + V tile
+constexpr int kWarps = kKvHeads;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kWaitPolls = 1u << 24;
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
+constexpr float kWeightShift = 15.0f;                       // P scaled by 2^15 before FP16
+constexpr int kPartialFloats = kQueryHeads * (kHeadDim + 2);
+
+template <int STAGES>
+constexpr int smem_bytes() {
+    return kWarps * STAGES * kStageBytes + 1024;  // + alignment slack
+}
+
+__device__ __forceinline__ float warp_max8(float v) {
+    // Reduce over the 8 lanes that share lane % 4 (the token rows of a fragment).
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum8(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    return v;
+}
+
+// Fetch one block's K and V boxes of KV head `head` into a pipeline stage
+// (called by one lane).  An out-of-range block id sets the error flag and
+// completes the stage's phase without data, so no waiter is left behind.
+__device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t block, int32_t num_blocks,
+                                            int32_t k_rows, int32_t v_rows, int head, uint32_t dst,
+                                            uint32_t bar, int32_t *error_flag) {
+    if (block < 0 || block >= num_blocks) {
+        atomicOr(error_flag, PKV_DEVICE_BAD_BLOCK);
+        pkv::mbar_arrive(bar);
+        return;
+    }
+    pkv::mbar_arrive_expect_tx(bar, kStageBytes);
+    pkv::tma_load_3d(dst, map, 0, head, k_rows + block * kBlockTokens, bar);
+    pkv::tma_load_3d(dst + kTileBytes, map, 0, head, v_rows + block * kBlockTokens, bar);
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
+    const __grid_constant__ CUtensorMap pool_map, const __half *__restrict__ query,
+    int64_t query_stride, const int32_t *__restrict__ lengths, const int32_t *__restrict__ prefix,
+    const int32_t *__restrict__ flat, int32_t batch, int32_t total_blocks, int32_t blocks_per_cta,
+    int32_t num_blocks, int32_t layer, __half *__restrict__ out, int64_t out_stride,
+    float *__restrict__ part_o, float *__restrict__ part_ml, int32_t *__restrict__ error_flag) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
+
+    const int begin = blockIdx.x * blocks_per_cta;
+    const int end = min(begin + blocks_per_cta, total_blocks);
+    if (begin >= end) return;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2;  // fragment row group
+    const int t = lane & 3;   // fragment column pair
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const uint32_t tiles = pkv::smem_addr(smem + warp * STAGES * kStageBytes);
+    const uint32_t bar0 = pkv::smem_addr(&barriers[warp * kMaxStages]);
+
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) pkv::mbar_init(bar0 + 8 * s, 1);
+        pkv::fence_barrier_init();
+    }
+    __syncwarp();
+
+    // Rows of this head's K and V boxes in the 3-D view of the pool
+    // (dim 64, kv head 4, pool row = ((layer*2 + kv)*num_blocks + block)*16).
+    const int32_t k_rows = (layer * 2 + 0) * num_blocks * kBlockTokens;
+    const int32_t v_rows = (layer * 2 + 1) * num_blocks * kBlockTokens;
+
+    // Producer state (used by lane 0 only): the next global block to fetch.
+    int next_fetch = begin;
+    if (lane == 0) {
+        const int n = min(STAGES, end - begin);
+        for (int s = 0; s < n; ++s) {
+            issue_block(&pool_map, flat[next_fetch], num_blocks, k_rows, v_rows, warp,
+                        tiles + s * kStageBytes, bar0 + 8 * s, error_flag);
+            ++next_fetch;
+        }
+    }
+
+    // First row of the range: the largest b with prefix[b] <= begin.
+    int lo = 0, hi = batch - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= begin) lo = mid; else hi = mid - 1;
+    }
+
+    int consumed = 0;
+    bool failed = false;
+    for (int row = lo, i = begin; i < end; ++row) {
+        const int row_first = prefix[row];
+        const int row_last = prefix[row + 1];
+        const int seg_end = min(end, row_last);
+        const int length = lengths[row];
+
+        // Q^T fragments (B operand) of this warp's 8 query heads.
+        const __half *q = query + row * query_stride + (warp * kGroup + g) * kHeadDim;
+        uint32_t qf[4][2];
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            qf[ks][0] = *reinterpret_cast<const uint32_t *>(q + 16 * ks + 2 * t);
+            qf[ks][1] = *reinterpret_cast<const uint32_t *>(q + 16 * ks + 8 + 2 * t);
+        }
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        float o[4][4];
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+        for (; i < seg_end; ++i, ++consumed) {
+            const int stage = consumed % STAGES;
+            const uint32_t parity = (consumed / STAGES) & 1;
+            if (!pkv::mbar_wait_bounded(bar0 + 8 * stage, parity, kWaitPolls)) {
+                failed = true;
+                break;
+            }
+            const uint32_t ktile = tiles + stage * kStageBytes;
+            const uint32_t vtile = ktile + kTileBytes;
+            const int valid = min(kBlockTokens, length - (i - row_first) * kBlockTokens);
+            if (valid < kBlockTokens) {
+                // Zero the V rows of unwritten slots: P is 0 there, but 0 * NaN is NaN.
+                uint8_t *vrows = smem + warp * STAGES * kStageBytes + stage * kStageBytes + kTileBytes;
+                for (int idx = lane; idx < (kBlockTokens - valid) * 8; idx += 32) {
+                    *reinterpret_cast<uint4 *>(vrows + (valid + idx / 8) * kRowBytes + (idx % 8) * 16) =
+                        make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
+            }
+
+            // S^T = K . Q^T over 64 dims (4 k-steps).
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                const int mat = lane >> 3;
+                const int tok = (lane & 7) + ((mat & 1) << 3);
+                const int chunk = 2 * ks + (mat >> 1);
+                uint32_t a0, a1, a2, a3;
+                pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), a0, a1, a2, a3);
+                pkv::mma_f16_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            }
+            // s[0]: (token g, head 2t), s[1]: (g, 2t+1), s[2]: (g+8, 2t), s[3]: (g+8, 2t+1)
+            const float s0 = g < valid ? s[0] * kScaleLog2 : -INFINITY;
+            const float s1 = g < valid ? s[1] * kScaleLog2 : -INFINITY;
+            const float s2 = g + 8 < valid ? s[2] * kScaleLog2 : -INFINITY;
+            const float s3 = g + 8 < valid ? s[3] * kScaleLog2 : -INFINITY;
+            const float mn0 = fmaxf(m0, warp_max8(fmaxf(s0, s2)));
+            const float mn1 = fmaxf(m1, warp_max8(fmaxf(s1, s3)));
+            const float alpha0 = pkv::exp2_approx(m0 - mn0);
+            const float alpha1 = pkv::exp2_approx(m1 - mn1);
+            m0 = mn0;
+            m1 = mn1;
+            const __half2 p01 = __floats2half2_rn(pkv::exp2_approx(s0 - mn0 + kWeightShift),
+                                                  pkv::exp2_approx(s1 - mn1 + kWeightShift));
+            const __half2 p23 = __floats2half2_rn(pkv::exp2_approx(s2 - mn0 + kWeightShift),
+                                                  pkv::exp2_approx(s3 - mn1 + kWeightShift));
+            const float2 f01 = __half22float2(p01);
+            const float2 f23 = __half22float2(p23);
+            l0 = l0 * alpha0 + (f01.x + f23.x);
+            l1 = l1 * alpha1 + (f01.y + f23.y);
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                o[mt][0] *= alpha0;
+                o[mt][1] *= alpha1;
+                o[mt][2] *= alpha0;
+                o[mt][3] *= alpha1;
+            }
+            // P^T fragments: transpose the (token x head) 8x8 halves.
+            const uint32_t b0 = pkv::movmatrix_trans(pkv::pack_half2(p01));
+            const uint32_t b1 = pkv::movmatrix_trans(pkv::pack_half2(p23));
+
+            // O^T += V^T . P^T over 16 tokens (4 dim tiles of 16).
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int mat = lane >> 3;
+                const int tok = (lane & 7) + ((mat >> 1) << 3);
+                const int chunk = 2 * mt + (mat & 1);
+                uint32_t a0, a1, a2, a3;
+                pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), a0, a1, a2, a3);
+                pkv::mma_f16_16816(o[mt], a0, a1, a2, a3, b0, b1);
+            }
+            // Every lane's shared-memory reads (and the zeroing writes) of this
+            // stage are ordered before the TMA that refills it.
+            pkv::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && next_fetch < end) {
+                issue_block(&pool_map, flat[next_fetch], num_blocks, k_rows, v_rows, warp,
+                            ktile, bar0 + 8 * stage, error_flag);
+                ++next_fetch;
+            }
+        }
+        if (failed) break;
+
+        l0 = warp_sum8(l0);
+        l1 = warp_sum8(l1);
+        const int head0 = warp * kGroup + 2 * t;  // heads of o[.][0|2] and o[.][1|3]
+        const int cta_first = row_first / blocks_per_cta;
+        const int cta_last = (row_last - 1) / blocks_per_cta;
+        if (cta_first == cta_last) {
+            __half *dst = out + row * out_stride;
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int d = 16 * mt + g;
+                dst[head0 * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][0], l0));
+                dst[(head0 + 1) * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][1], l1));
+                dst[head0 * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][2], l0));
+                dst[(head0 + 1) * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][3], l1));
+            }
+        } else {
+            const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
+            float *po = part_o + index * kQueryHeads * kHeadDim;
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int d = 16 * mt + g;
+                po[head0 * kHeadDim + d] = o[mt][0];
+                po[(head0 + 1) * kHeadDim + d] = o[mt][1];
+                po[head0 * kHeadDim + d + 8] = o[mt][2];
+                po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
+            }
+            if (g == 0) {
+                float *pml = part_ml + index * kQueryHeads * 2;
+                pml[head0 * 2 + 0] = m0;
+                pml[head0 * 2 + 1] = l0;
+                pml[(head0 + 1) * 2 + 0] = m1;
+                pml[(head0 + 1) * 2 + 1] = l1;
+            }
+        }
+    }
+
+    if (failed) {
+        if (lane == 0) atomicOr(error_flag, PKV_DEVICE_WAIT_TIMEOUT);
+        // Let the copies this warp issued finish before its shared memory is released.
+        for (int c = consumed; c < next_fetch - begin; ++c) {
+            pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
+        }
+    }
+}
+
+// One warp per (row, query head) of a split row: merge its partials.
+__global__ void __launch_bounds__(256) decode_combine_kernel(
+    const float *__restrict__ part_o, const float *__restrict__ part_ml,
+    const int32_t *__restrict__ prefix, int32_t batch, int32_t blocks_per_cta,
+    __half *__restrict__ out, int64_t out_stride) {
+    const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int row = pair / kQueryHeads;
+    const int head = pair % kQueryHeads;
+    if (row >= batch) return;
+    const int cta_first = prefix[row] / blocks_per_cta;
+    const int cta_last = (prefix[row + 1] - 1) / blocks_per_cta;
+    if (cta_first == cta_last) return;  // written directly by the split kernel
+    float m = -INFINITY;
+    for (int c = cta_first; c <= cta_last; ++c) {
+        m = fmaxf(m, part_ml[((static_cast<int64_t>(row) + c) * kQueryHeads + head) * 2]);
+    }
+    float l = 0.f, acc0 = 0.f, acc1 = 0.f;
+    for (int c = cta_first; c <= cta_last; ++c) {
+        const int64_t index = static_cast<int64_t>(row) + c;
+        const float *ml = part_ml + (index * kQueryHeads + head) * 2;
+        const float w = pkv::exp2_approx(ml[0] - m);
+        l += ml[1] * w;
+        const float2 v = *reinterpret_cast<const float2 *>(
+            part_o + (index * kQueryHeads + head) * kHeadDim + 2 * lane);
+        acc0 += v.x * w;
+        acc1 += v.y * w;
+    }
+    *reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + 2 * lane) =
+        __floats2half2_rn(__fdiv_rn(acc0, l), __fdiv_rn(acc1, l));
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor-map cache, launch plan, entry point.
+// ---------------------------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            p = nullptr;
+        }
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    return fn;
+}
+
+struct MapKey {
+    uintptr_t pool;
+    int32_t blocks;
+    bool operator==(const MapKey &o) const { return pool == o.pool && blocks == o.blocks; }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const { return std::hash<uintptr_t>()(k.pool) ^ (size_t(k.blocks) << 1); }
+};
+
+// 3-D view of the pool for per-head boxes: (dim 64, kv head 4, pool row),
+// strides 128 B (head) and 512 B (row), box 64 x 1 x 16 with the 128-byte
+// swizzle.  Cached per (pool address, block count); the map depends on
+// nothing else.
+int pool_tensor_map(const void *pool, int32_t num_blocks, CUtensorMap *out) {
+    static std::mutex mutex;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{reinterpret_cast<uintptr_t>(pool), num_blocks};
+    std::lock_guard<std::mutex> lock(mutex);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return PKV_OK;
+    }
+    EncodeTiled encode = encode_fn();
+    if (encode == nullptr) return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t rows = static_cast<cuuint64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(kKvHeads), rows};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kRowBytes),
+                                   static_cast<cuuint64_t>(kKvHeads * kRowBytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHeadDim), 1u, static_cast<cuuint32_t>(kBlockTokens)};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    CUtensorMap map;
+    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(pool), dims,
+                              strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    }
+    cache.emplace(key, map);
+    *out = map;
+    return PKV_OK;
+}
+
+// Pipeline depth per warp; PKV_DECODE_STAGES (4, 6 or 8) overrides it.
+int configured_stages() {
+    static int stages = [] {
+        const char *env = std::getenv("PKV_DECODE_STAGES");
+        const int v = env ? std::atoi(env) : 6;
+        return (v == 4 || v == 6 || v == 8) ? v : 6;
+    }();
+    return stages;
+}
+
+template <int STAGES>
+int prepare_kernel(int *ctas_per_sm) {
+    auto kernel = decode_attention_kernel<STAGES>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<STAGES>());
+    if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, kThreads, smem_bytes<STAGES>());
+    if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("occupancy query: ") + cudaGetErrorString(e));
+    return PKV_OK;
+}
+
+struct DeviceInfo {
+    int sms = 0;
+    int ctas_per_sm = 0;
+};
+
+int device_info(int device, DeviceInfo *info) {
+    static std::mutex mutex;
+    static std::unordered_map<int, DeviceInfo> cache;
+    std::lock_guard<std::mutex> lock(mutex);
+    auto it = cache.find(device * 16 + configured_stages());
+    if (it != cache.end()) {
+        *info = it->second;
+        return PKV_OK;
+    }
+    int previous = 0;
+    cudaGetDevice(&previous);
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    DeviceInfo d;
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
+    int rc = PKV_OK;
+    switch (configured_stages()) {
+        case 4: rc = prepare_kernel<4>(&d.ctas_per_sm); break;
+        case 8: rc = prepare_kernel<8>(&d.ctas_per_sm); break;
+        default: rc = prepare_kernel<6>(&d.ctas_per_sm); break;
+    }
+    cudaSetDevice(previous);
+    if (rc) return rc;
+    if (d.ctas_per_sm < 1) d.ctas_per_sm = 1;
+    cache.emplace(device * 16 + configured_stages(), d);
+    *info = d;
+    return PKV_OK;
+}
+
+}  // namespace
+
+extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
+                               int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes) {
+    pkv::clear_error();
+    if (batch < 1 || total_blocks < batch) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode plan needs batch >= 1 and a nonempty block per row");
+    }
+    DeviceInfo info;
+    int rc = device_info(device, &info);
+    if (rc) return rc;
+    const int64_t slots = static_cast<int64_t>(info.sms) * info.ctas_per_sm;
+    const int32_t per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
+    const int32_t grid = (total_blocks + per_cta - 1) / per_cta;
+    *out_grid = grid;
+    *out_blocks_per_cta = per_cta;
+    *out_workspace_bytes = (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
+    return PKV_OK;
+}
+
+extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer,
+                                    const void *query, int64_t query_stride, const int32_t *lengths,
+                                    const int32_t *prefix, const int32_t *flat, int32_t batch,
+                                    int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                    void *out, int64_t out_stride, void *workspace,
+                                    int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    if (pool == nullptr || query == nullptr || lengths == nullptr || prefix == nullptr ||
+        flat == nullptr || out == nullptr || error_flag == nullptr) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: null pointer argument");
+    }
+    if (layer < 0 || layer >= PKV_LAYERS) {
+        return pkv::fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
+    }
+    if (batch < 1 || total_blocks < batch || grid < 1 || blocks_per_cta < 1 ||
+        static_cast<int64_t>(grid) * blocks_per_cta < total_blocks ||
+        static_cast<int64_t>(grid - 1) * blocks_per_cta >= total_blocks) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: launch plan does not match the batch");
+    }
+    if (num_blocks < 1 || static_cast<int64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens > INT32_MAX) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: pool block count out of range");
+    }
+    if ((reinterpret_cast<uintptr_t>(query) & 3) || (reinterpret_cast<uintptr_t>(out) & 3) ||
+        query_stride % 2 || out_stride % 2 || (reinterpret_cast<uintptr_t>(pool) & 15) ||
+        (reinterpret_cast<uintptr_t>(workspace) & 15)) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: misaligned tensor");
+    }
+    const int64_t needed = (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
+    const bool any_split = grid > 1 && total_blocks > blocks_per_cta;
+    if (any_split && (workspace == nullptr || workspace_bytes < needed)) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: workspace is smaller than the plan needs");
+    }
+    int device = 0;
+    cudaGetDevice(&device);
+    DeviceInfo info;
+    int rc = device_info(device, &info);
+    if (rc) return rc;
+    CUtensorMap map;
+    if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
+    float *part_o = static_cast<float *>(workspace);
+    float *part_ml = part_o ? part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const __half *q = static_cast<const __half *>(query);
+    __half *o = static_cast<__half *>(out);
+    switch (configured_stages()) {
+        case 4:
+            decode_attention_kernel<4><<<grid, kThreads, smem_bytes<4>(), s>>>(
+                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
+                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
+            break;
+        case 8:
+            decode_attention_kernel<8><<<grid, kThreads, smem_bytes<8>(), s>>>(
+                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
+                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
+            break;
+        default:
+            decode_attention_kernel<6><<<grid, kThreads, smem_bytes<6>(), s>>>(
+                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
+                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
+            break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        return pkv::fail(PKV_CUDA_ERROR, std::string("decode attention launch failed: ") + cudaGetErrorString(e));
+    }
+    if (any_split) {
+        const int warps_per_cta = 8;
+        const int pairs = batch * kQueryHeads;
+        decode_combine_kernel<<<(pairs + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(
+            part_o, part_ml, prefix, batch, blocks_per_cta, o, out_stride);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
+        }
+    }
+    return PKV_OK;
+}

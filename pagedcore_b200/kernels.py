@@ -1,0 +1,175 @@
+"""Torch-tensor wrappers of the device entry points of ``libpagedkv.so``.
+
+These functions only check tensor properties and pass raw pointers, sizes and
+the current CUDA stream across the C ABI; all device work is done by the
+sm_100a kernels in ``csrc/``.  Every function raises if the library is
+missing or a tensor is not on a CUDA device: there is no non-native path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from pagedcore_b200._lib import check, lib
+
+_LAYERS = 22
+_KV_HEADS = 4
+_QUERY_HEADS = 32
+_HEAD_DIM = 64
+
+
+def _ptr(tensor: Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if tensor is None else tensor.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(name: str, tensor: Tensor, device: torch.device) -> None:
+    if tensor.device != device or tensor.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor on {device}")
+
+
+def _kv_rows_ok(tensor: Tensor) -> bool:
+    """Inner [4, 64] contiguous and 16-byte aligned rows, as the kernel reads them."""
+    return (
+        tensor.stride(2) == _HEAD_DIM
+        and tensor.stride(3) == 1
+        and tensor.stride(0) % 8 == 0
+        and tensor.stride(1) % 8 == 0
+        and tensor.data_ptr() % 16 == 0
+    )
+
+
+def append_kv(
+    pool: Tensor,
+    key: Tensor,
+    value: Tensor,
+    slots: Tensor,
+    *,
+    layer_begin: int,
+    error_flag: Tensor,
+    positions: Tensor | None = None,
+    rope_table: Tensor | None = None,
+    query_in: Tensor | None = None,
+    query_out: Tensor | None = None,
+) -> None:
+    """Scatter FP16 K/V [layers, tokens, 4, 64] into the pool at ``slots``.
+
+    With ``rope_table`` the K rows (and ``query_in`` [layers, tokens, 32, 64],
+    written rotated to ``query_out``) are rotated at ``positions`` first.
+    """
+    device = pool.device
+    for name, tensor in (("key", key), ("value", value), ("slots", slots), ("error_flag", error_flag)):
+        _require_cuda(name, tensor, device)
+    if key.ndim != 4 or key.shape[2:] != (_KV_HEADS, _HEAD_DIM) or value.shape != key.shape:
+        raise ValueError("K and V must share FP16 [layers, tokens, 4, 64]")
+    if key.dtype != torch.float16 or value.dtype != torch.float16:
+        raise ValueError("K and V must be FP16")
+    if not (_kv_rows_ok(key) and value.stride() == key.stride()):
+        key, value = key.contiguous(), value.contiguous()
+    layers, tokens = key.shape[0], key.shape[1]
+    if slots.dtype != torch.int32 or slots.numel() < tokens:
+        raise ValueError("slots must be int32 with one entry per token")
+    if query_in is not None:
+        if query_out is None or query_in.shape != (layers, tokens, _QUERY_HEADS, _HEAD_DIM):
+            raise ValueError("query must be FP16 [layers, tokens, 32, 64] with an output buffer")
+        query_in = query_in.contiguous()
+        if query_out.shape != query_in.shape or not query_out.is_contiguous():
+            raise ValueError("query_out must be a contiguous buffer shaped like query")
+    check(
+        lib.pkv_append_kv(
+            _ptr(pool),
+            pool.shape[2],
+            layer_begin,
+            layers,
+            _ptr(key),
+            _ptr(value),
+            key.stride(0),
+            key.stride(1),
+            _ptr(slots),
+            _ptr(positions),
+            tokens,
+            _ptr(rope_table),
+            _ptr(query_in),
+            _ptr(query_out),
+            0 if query_in is None else query_in.stride(0),
+            0 if query_in is None else query_in.stride(1),
+            _ptr(error_flag),
+            _stream(device),
+        )
+    )
+
+
+@dataclass(frozen=True, slots=True)
+class DecodePlan:
+    grid: int
+    blocks_per_cta: int
+    workspace_bytes: int
+
+
+def decode_plan(device: torch.device, batch: int, total_blocks: int) -> DecodePlan:
+    grid = ctypes.c_int32()
+    per_cta = ctypes.c_int32()
+    workspace = ctypes.c_int64()
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    check(
+        lib.pkv_decode_plan(
+            index, batch, total_blocks, ctypes.byref(grid), ctypes.byref(per_cta), ctypes.byref(workspace)
+        )
+    )
+    return DecodePlan(grid.value, per_cta.value, workspace.value)
+
+
+def decode_attention(
+    pool: Tensor,
+    layer: int,
+    query: Tensor,
+    lengths: Tensor,
+    prefix: Tensor,
+    flat: Tensor,
+    total_blocks: int,
+    plan: DecodePlan,
+    out: Tensor,
+    workspace: Tensor | None,
+    error_flag: Tensor,
+) -> Tensor:
+    """Split-K block-table attention of FP16 query [B, 32, 64] into ``out``."""
+    device = pool.device
+    batch = query.shape[0]
+    if query.ndim != 3 or query.shape[1:] != (_QUERY_HEADS, _HEAD_DIM) or query.dtype != torch.float16:
+        raise ValueError("query must be FP16 [batch, 32, 64]")
+    if query.stride()[1:] != (_HEAD_DIM, 1):
+        query = query.contiguous()
+    if out.shape != query.shape or out.dtype != torch.float16 or out.stride()[1:] != (_HEAD_DIM, 1):
+        raise ValueError("out must be FP16 [batch, 32, 64] with contiguous rows")
+    for name, tensor in (("query", query), ("out", out), ("lengths", lengths), ("prefix", prefix), ("flat", flat)):
+        _require_cuda(name, tensor, device)
+    check(
+        lib.pkv_decode_attention(
+            _ptr(pool),
+            pool.shape[2],
+            layer,
+            _ptr(query),
+            query.stride(0),
+            _ptr(lengths),
+            _ptr(prefix),
+            _ptr(flat),
+            batch,
+            total_blocks,
+            plan.grid,
+            plan.blocks_per_cta,
+            _ptr(out),
+            out.stride(0),
+            _ptr(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            _ptr(error_flag),
+            _stream(device),
+        )
+    )
+    return out

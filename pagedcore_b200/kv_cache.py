@@ -1,0 +1,459 @@
+"""Drop-in KV pool and allocator for PagedCore's paged KV path on B200.
+
+Same API, argument meaning and exception contract as
+src/pagedcore/kv_cache.py: ``allocate_kv_pool`` (17-47) and ``KVAllocator``
+(63-357).  The bookkeeping lives in the C++ ledger (``csrc/ledger.cpp``) and
+every K/V write is the sm_100a scatter kernel (``csrc/append_kv.cu``); this
+module only validates arguments in the reference's order, maps request ids to
+ledger handles and passes device pointers across the C ABI.
+
+Differences from the reference, by design:
+- the pool must be CUDA storage (the reference also accepts CPU pools for its
+  own allocator tests; the bookkeeping alone is :class:`BlockLedger`);
+- ``validation="incremental"`` replaces the O(pool) re-validation on every
+  call by a check of the touched requests (the default stays "full");
+- batched entry points for the decode hot path: ``write_decode_batch``,
+  ``append(..., rotate=True)`` with K-RoPE fused, and ``decode_batch`` which
+  returns the device-side block tables of a batch.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterator, Sequence
+from contextlib import contextmanager
+from dataclasses import dataclass
+from threading import current_thread
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from pagedcore_b200 import kernels
+from pagedcore_b200._lib import device_error_message
+from pagedcore_b200.config import PagedCoreConfig
+from pagedcore_b200.engine_types import BlockId, BlockTable, CapacityCounts, KVReservation, RequestId
+from pagedcore_b200.ledger import BlockLedger
+from pagedcore_b200.rope import device_table
+
+_LAYERS = 22
+_BLOCK_TOKENS = 16
+_UNKNOWN_BASE = -(1 << 62)
+
+
+def allocate_kv_pool(config: PagedCoreConfig, *, device: str | torch.device = "cuda:0") -> Tensor:
+    """Allocate the FP16 [22, 2, blocks, 16, 4, 64] pool once (kv_cache.py:17-47).
+
+    Storage is uninitialised: only written, valid slots may be read.
+    """
+    target = torch.device(device)
+    if target.type != "cuda":
+        raise ValueError("KV pool requires a CUDA device")
+    if not torch.cuda.is_available():
+        raise RuntimeError("KV pool requires an available CUDA runtime")
+    pool_bytes = config.kv_pool_mib * 2**20
+    margin_bytes = config.workspace_margin_mib * 2**20
+    block_bytes = _LAYERS * 2 * config.block_tokens * 4 * 64 * 2
+    num_blocks = pool_bytes // block_bytes
+    free_bytes, _ = torch.cuda.mem_get_info(target)
+    if free_bytes < pool_bytes + margin_bytes:
+        raise RuntimeError("configured KV pool and workspace margin do not fit in GPU memory")
+    pool = torch.empty(
+        (_LAYERS, 2, num_blocks, config.block_tokens, 4, 64), dtype=torch.float16, device=target
+    )
+    if torch.cuda.mem_get_info(target)[0] < margin_bytes:
+        del pool
+        raise RuntimeError("KV pool allocation leaves less than the configured workspace margin")
+    return pool
+
+
+@dataclass(slots=True)
+class DecodeBatch:
+    """Device-resident block tables of a batch: what the attention kernel reads.
+
+    ``lengths`` [B], ``prefix`` [B+1] (cumulative block counts) and ``flat``
+    (the concatenated tables) are views of one int32 device buffer.
+    """
+
+    requests: tuple[RequestId, ...]
+    lengths: Tensor
+    prefix: Tensor
+    flat: Tensor
+    total_blocks: int
+    plan: kernels.DecodePlan
+    host_lengths: np.ndarray
+
+
+@dataclass(slots=True)
+class _Staged:
+    requests: tuple[RequestId, ...]
+    handles: np.ndarray
+    rows: dict[RequestId, int]
+    slots: Tensor  # int32 device [B]
+    positions: Tensor  # int32 device [B]
+    host_positions: np.ndarray
+    written: int = 0  # layers written for every row by write_decode_batch
+    batch: DecodeBatch | None = None
+
+
+class KVAllocator:
+    """Assign blocks within an existing CUDA pool (kv_cache.py:63-90).
+
+    Construct and use on the model worker thread; CUDA work stays on the
+    stream current at construction.  Block reads borrow pool storage.
+    """
+
+    def __init__(self, pool: Tensor, *, validation: str = "full") -> None:
+        if (
+            pool.ndim != 6
+            or pool.shape[:2] != (22, 2)
+            or pool.shape[2] < 1
+            or pool.shape[3:] != (16, 4, 64)
+            or pool.dtype != torch.float16
+            or pool.device.type not in ("cpu", "cuda")
+            or not pool.is_contiguous()
+            or pool.requires_grad
+        ):
+            raise ValueError("KV pool must be contiguous FP16 [22, 2, blocks, 16, 4, 64] storage")
+        if pool.device.type != "cuda":
+            raise ValueError("KV pool must be CUDA storage: the B200 KV path has no CPU implementation")
+        self._pool = pool
+        self._worker = current_thread()
+        self._stream = torch.cuda.current_stream(pool.device)
+        self._ledger = BlockLedger(pool.shape[2], validation)
+        self._handles: dict[RequestId, int] = {}
+        self._next_handle = 1
+        self._staged: _Staged | None = None
+        self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
+        self._rope = device_table(pool.device)
+        self._workspace: Tensor | None = None
+
+    # -- plumbing -------------------------------------------------------------
+    @property
+    def pool(self) -> Tensor:
+        return self._pool
+
+    @property
+    def ledger(self) -> BlockLedger:
+        return self._ledger
+
+    def _check_worker(self) -> None:
+        if current_thread() is not self._worker:
+            raise RuntimeError("KV allocator must be used by its owning model worker")
+        if torch.cuda.current_stream(self._pool.device) != self._stream:
+            raise RuntimeError("KV allocator must use its owning CUDA stream")
+
+    def _handle(self, request_id: RequestId, unknown_index: int = 0) -> int:
+        handle = self._handles.get(request_id)
+        return handle if handle is not None else _UNKNOWN_BASE - unknown_index
+
+    def _call(self, function, request_id: RequestId | None, *args):
+        try:
+            return function(*args)
+        except KeyError:
+            raise KeyError(request_id) from None
+
+    def _upload_i32(self, *arrays: np.ndarray) -> Tensor:
+        """One pinned host->device copy of several int32 arrays, concatenated."""
+        host = torch.empty(sum(len(a) for a in arrays), dtype=torch.int32, pin_memory=True)
+        view = host.numpy()
+        offset = 0
+        for array in arrays:
+            view[offset : offset + len(array)] = array
+            offset += len(array)
+        return host.to(self._pool.device, non_blocking=True)
+
+    def _workspace_for(self, nbytes: int) -> Tensor | None:
+        if nbytes <= 0:
+            return None
+        if self._workspace is None or self._workspace.numel() * 4 < nbytes:
+            self._workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
+        return self._workspace
+
+    def check_device_errors(self) -> None:
+        """Synchronise and raise if a kernel flagged an out-of-range block or position."""
+        flag = int(self._error.item())
+        if flag:
+            self._error.zero_()
+            raise RuntimeError(device_error_message(flag))
+
+    # -- reference API ----------------------------------------------------------
+    def create(self, reservation: KVReservation) -> None:
+        """Grant credits at admission without assigning blocks (kv_cache.py:92-110)."""
+        self._check_worker()
+        request_id = reservation.request_id
+        handle = self._handles.get(request_id)
+        if handle is None:
+            handle = self._next_handle
+        self._ledger.reserve(handle, reservation.maximum_block_credits)
+        if request_id not in self._handles:
+            self._handles[request_id] = handle
+            self._next_handle += 1
+
+    def capacity(self) -> CapacityCounts:
+        self._check_worker()
+        return CapacityCounts(*self._ledger.capacity())
+
+    def block_table(self, request_id: RequestId) -> BlockTable:
+        self._check_worker()
+        table = self._call(self._ledger.table, request_id, self._handle(request_id))
+        return tuple(BlockId(block) for block in table)
+
+    def cached_length(self, request_id: RequestId) -> int:
+        self._check_worker()
+        return self._call(self._ledger.length, request_id, self._handle(request_id))
+
+    @torch.inference_mode()
+    def append(self, request_id: RequestId, key: Tensor, value: Tensor, *, rotate: bool = False) -> None:
+        """Append rotated K and unrotated V, each FP16 [22, tokens, 4, 64] (kv_cache.py:127-179).
+
+        With ``rotate=True`` K is given unrotated and the kernel applies RoPE at
+        the absolute positions it is written to.  A failed launch leaves
+        ownership and valid positions unchanged.
+        """
+        self._check_worker()
+        if self._ledger.staging:
+            raise RuntimeError("KV mutation is not allowed during a staged decode append")
+        handle = self._handle(request_id)
+        self._call(self._ledger.length, request_id, handle)
+        if (
+            key.ndim != 4
+            or key.shape[0] != 22
+            or key.shape[1] < 1
+            or key.shape[2:] != (4, 64)
+            or value.shape != key.shape
+            or key.dtype != torch.float16
+            or value.dtype != torch.float16
+            or key.device != self._pool.device
+            or value.device != self._pool.device
+        ):
+            raise ValueError("K and V must share FP16 [22, tokens, 4, 64] on the pool device")
+        tokens = key.shape[1]
+        slots, start = self._call(self._ledger.append_plan, request_id, handle, tokens)
+        if rotate:
+            positions = np.arange(start, start + tokens, dtype=np.int32)
+            meta = self._upload_i32(slots, positions)
+            kernels.append_kv(
+                self._pool, key, value, meta[:tokens], layer_begin=0, error_flag=self._error,
+                positions=meta[tokens:], rope_table=self._rope,
+            )
+        else:
+            meta = self._upload_i32(slots)
+            kernels.append_kv(self._pool, key, value, meta, layer_begin=0, error_flag=self._error)
+        # Publish valid positions only after both K and V writes were issued.
+        self._ledger.append_commit(handle, tokens)
+
+    @contextmanager
+    def append_decode(self, request_ids: tuple[RequestId, ...]) -> Iterator[None]:
+        """Stage one token per request; commit all 22 layers together (kv_cache.py:181-219)."""
+        self._check_worker()
+        if self._ledger.staging:
+            raise RuntimeError("KV mutation is not allowed during a staged decode append")
+        request_ids = tuple(request_ids)
+        unknown = 0
+        handles = np.empty(len(request_ids), dtype=np.int64)
+        for row, request_id in enumerate(request_ids):
+            handle = self._handles.get(request_id)
+            if handle is None:
+                unknown += 1
+                handle = _UNKNOWN_BASE - unknown
+            handles[row] = handle
+        try:
+            slots, positions = self._ledger.decode_begin(handles)
+        except KeyError as error:
+            missing = next((r for r in request_ids if r not in self._handles), None)
+            raise KeyError(missing) from error
+        meta = self._upload_i32(slots, positions)
+        count = len(request_ids)
+        self._staged = _Staged(
+            requests=request_ids,
+            handles=handles,
+            rows={request_id: row for row, request_id in enumerate(request_ids)},
+            slots=meta[:count],
+            positions=meta[count:],
+            host_positions=positions,
+        )
+        try:
+            yield
+        except BaseException:
+            self._ledger.decode_abort()
+            raise
+        else:
+            self._ledger.decode_commit()
+        finally:
+            self._staged = None
+
+    @torch.inference_mode()
+    def write_decode_layer(self, request_id: RequestId, layer_index: int, key: Tensor, value: Tensor) -> None:
+        """Write one token's rotated K / unrotated V [4, 64], in layer order (kv_cache.py:221-246)."""
+        self._check_worker()
+        staged = self._staged
+        layer = layer_index if type(layer_index) is int else -1
+        handle = self._handle(request_id)
+        self._call(self._ledger.decode_check, request_id, handle, layer)
+        if any(
+            tensor.shape != (4, 64) or tensor.dtype != torch.float16 or tensor.device != self._pool.device
+            for tensor in (key, value)
+        ):
+            raise ValueError("K and V must share FP16 [4, 64] on the pool device")
+        row = staged.rows[request_id]
+        kernels.append_kv(
+            self._pool, key[None, None], value[None, None], staged.slots[row : row + 1],
+            layer_begin=layer, error_flag=self._error,
+        )
+        self._ledger.decode_mark(handle, layer)
+
+    @torch.inference_mode()
+    def write_decode_batch(
+        self,
+        layer_index: int,
+        key: Tensor,
+        value: Tensor,
+        *,
+        query: Tensor | None = None,
+        rotate: bool = False,
+    ) -> Tensor | None:
+        """Batched ``write_decode_layer`` for every staged request, in staging order.
+
+        key/value: FP16 [B, 4, 64] (unrotated K when ``rotate``).  With
+        ``query`` [B, 32, 64] and ``rotate=True`` the rotated query is returned
+        (RoPE of Q and K fused into the append kernel).
+        """
+        self._check_worker()
+        staged = self._staged
+        if staged is None:
+            raise RuntimeError("decode writes require a staged append")
+        layer = layer_index if type(layer_index) is int else -1
+        self._ledger.decode_check(-1, layer)
+        count = len(staged.requests)
+        if key.shape != (count, 4, 64) or value.shape != key.shape:
+            raise ValueError("K and V must share FP16 [batch, 4, 64] on the pool device")
+        query_out = None
+        if query is not None:
+            if not rotate:
+                raise ValueError("query is only accepted together with rotate=True")
+            if query.shape != (count, 32, 64) or query.dtype != torch.float16:
+                raise ValueError("query must be FP16 [batch, 32, 64]")
+            query_out = torch.empty((1, count, 32, 64), dtype=torch.float16, device=self._pool.device)
+        kernels.append_kv(
+            self._pool,
+            key[None],
+            value[None],
+            staged.slots,
+            layer_begin=layer,
+            error_flag=self._error,
+            positions=staged.positions if rotate else None,
+            rope_table=self._rope if rotate else None,
+            query_in=None if query is None else query[None],
+            query_out=query_out,
+        )
+        self._ledger.decode_mark(-1, layer)
+        staged.written = layer + 1
+        return None if query_out is None else query_out[0]
+
+    def decode_positions(self) -> np.ndarray:
+        """RoPE positions (cached lengths before the append) of the staged rows."""
+        if self._staged is None:
+            raise RuntimeError("decode writes require a staged append")
+        return self._staged.host_positions.copy()
+
+    def iter_layer_blocks(self, request_id: RequestId, *, layer_index: int) -> Iterator[tuple[Tensor, Tensor]]:
+        """Borrow valid [slots, 4, 64] pages, including a completed staged layer (kv_cache.py:248-270)."""
+        self._check_worker()
+        if type(layer_index) is not int or not 0 <= layer_index < _LAYERS:
+            raise ValueError("layer_index must identify one of the 22 decoder layers")
+        blocks, length = self._call(self._ledger.view, request_id, self._handle(request_id), layer_index)
+        if length == 0:
+            raise ValueError("attention requires a nonempty cache")
+        for logical, physical in enumerate(blocks):
+            self._check_worker()
+            valid = min(_BLOCK_TOKENS, length - logical * _BLOCK_TOKENS)
+            yield (
+                self._pool[layer_index, 0, physical, :valid],
+                self._pool[layer_index, 1, physical, :valid],
+            )
+
+    def read_block(self, request_id: RequestId, logical_block: int) -> tuple[Tensor, Tensor]:
+        """Borrow K/V views [22, valid slots, 4, 64] of one logical block (kv_cache.py:272-284)."""
+        self._check_worker()
+        handle = self._handle(request_id)
+        blocks = self._call(self._ledger.table, request_id, handle)
+        length = self._ledger.length(handle)
+        if type(logical_block) is not int or not 0 <= logical_block < len(blocks):
+            raise ValueError("logical block must identify a cached block")
+        physical = blocks[logical_block]
+        valid = min(_BLOCK_TOKENS, length - logical_block * _BLOCK_TOKENS)
+        return self._pool[:, 0, physical, :valid], self._pool[:, 1, physical, :valid]
+
+    def release_all(self, request_id: RequestId) -> None:
+        """Release once on the worker stream (kv_cache.py:286-298)."""
+        self._check_worker()
+        self._call(self._ledger.release, request_id, self._handle(request_id))
+        del self._handles[request_id]
+
+    # -- batched attention metadata ---------------------------------------------
+    def decode_batch(self, request_ids: Sequence[RequestId], *, layer_index: int) -> DecodeBatch:
+        """Device block tables, lengths and launch plan for a batch at ``layer_index``.
+
+        During a staged decode the staged rows expose their new token once the
+        layer was written.  The result is reused across layers of one staged
+        step (the tables do not change between layers).
+        """
+        self._check_worker()
+        if type(layer_index) is not int or not 0 <= layer_index < _LAYERS:
+            raise ValueError("layer_index must identify one of the 22 decoder layers")
+        request_ids = tuple(request_ids)
+        staged = self._staged
+        if (
+            staged is not None
+            and staged.batch is not None
+            and staged.batch.requests == request_ids
+            and layer_index < staged.written
+        ):
+            return staged.batch
+        handles = np.fromiter(
+            (self._handle(r, i + 1) for i, r in enumerate(request_ids)), dtype=np.int64, count=len(request_ids)
+        )
+        count = len(request_ids)
+        if count == 0:
+            raise ValueError("attention requires a nonempty batch")
+        host = np.empty(2 * count + 1 + 129 * count, dtype=np.int32)
+        try:
+            total = self._ledger.batch_into(handles, layer_index, host)
+        except KeyError as error:
+            missing = next((r for r in request_ids if r not in self._handles), None)
+            raise KeyError(missing) from error
+        used = 2 * count + 1 + total
+        device = self._upload_i32(host[:used])
+        plan = kernels.decode_plan(self._pool.device, count, total)
+        batch = DecodeBatch(
+            requests=request_ids,
+            lengths=device[:count],
+            prefix=device[count : 2 * count + 1],
+            flat=device[2 * count + 1 : used],
+            total_blocks=total,
+            plan=plan,
+            host_lengths=host[:count].copy(),
+        )
+        if staged is not None and request_ids == staged.requests and layer_index < staged.written:
+            staged.batch = batch
+        return batch
+
+    def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
+        """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""
+        self._check_worker()
+        if out is None:
+            out = torch.empty(query.shape, dtype=torch.float16, device=self._pool.device)
+        kernels.decode_attention(
+            self._pool,
+            layer_index,
+            query,
+            batch.lengths,
+            batch.prefix,
+            batch.flat,
+            batch.total_blocks,
+            batch.plan,
+            out,
+            self._workspace_for(batch.plan.workspace_bytes),
+            self._error,
+        )
+        return out

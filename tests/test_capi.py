@@ -1,0 +1,49 @@
+"""The C ABI surface: the library loads and exports what include/pagedkv.h declares."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+from pagedcore_b200 import _lib
+from tests.conftest import ROOT
+
+HEADER = ROOT / "include" / "pagedkv.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(pkv_[a-z0-9_]+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    declared = declared_functions()
+    assert len(declared) >= 25
+    library = ctypes.CDLL(str(_lib.LIBRARY_PATH))
+    missing = [name for name in sorted(declared) if not hasattr(library, name)]
+    assert missing == []
+
+
+def test_binding_covers_every_declared_symbol() -> None:
+    assert declared_functions() == set(_lib.SIGNATURES)
+
+
+def test_abi_version_and_error_channel() -> None:
+    assert _lib.lib.pkv_abi_version() == 1
+    assert _lib.lib.pkv_rope_table_bytes() == 2 * 2048 * 32 * 2
+    out = ctypes.c_void_p()
+    status = _lib.lib.pkv_ledger_new(0, 1, ctypes.byref(out))
+    assert status == _lib.PKV_VALUE_ERROR
+    assert b"KV pool must be contiguous" in _lib.lib.pkv_last_error()
+
+
+def test_device_entry_points_reject_bad_arguments_before_any_launch() -> None:
+    # Null pointers are refused on the host: no CUDA call is made.
+    status = _lib.lib.pkv_append_kv(None, 1, 0, 1, None, None, 0, 0, None, None, 1, None, None, None, 0, 0, None, None)
+    assert status == _lib.PKV_VALUE_ERROR
+    status = _lib.lib.pkv_decode_attention(
+        None, 1, 0, None, 0, None, None, None, 1, 1, 1, 1, None, 0, None, 0, None, None
+    )
+    assert status == _lib.PKV_VALUE_ERROR
+    assert b"null pointer" in _lib.lib.pkv_last_error()
