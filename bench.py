@@ -1,0 +1,468 @@
+"""Benchmark of the paged KV-cache hot path on B200.
+
+One step = one batched one-token decode step of the KV path over all 22
+layers for the rank's 256 sequences (contexts U[1, 2048-64], tables
+fragmented by allocator churn): staged append in the C++ ledger, then per
+layer the fused K/Q-RoPE + KV scatter kernel and the split-K GQA decode
+attention (+ combine), then the commit.  The dense TinyLlama GEMMs around it
+are not part of this path.  Sequences shard across GPUs with no collective
+(weak scaling: every rank owns 256 sequences and its own pool).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is decode tokens/s over all ranks with inputs resident in HBM;
+`e2e` is the same through the public API with host (pinned) inputs copied in
+and attention outputs copied out inside the timed region; `roofline` is the
+decode attention (split + combine launches) against the measured HBM copy
+bandwidth; `cpu_baseline` is the oracle port of the reference's CPU path on a
+bounded sample.  `--impl reference` times that CPU path alone on all host
+cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged decode-attn HBM GB/s (% of peak) and decode tokens/s at 1/2/4/8 B200"
+SEQUENCES = 256  # per GPU (config 4); --sequences overrides it for small profiling cases
+LAYERS = 22
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# CPU path: the oracle port of the reference (bench's CPU-baseline leg).
+# ---------------------------------------------------------------------------
+def oracle_decode_rows(lengths: list[int], num_blocks: int, steps: int, warmup: int, seed: int) -> float:
+    """Seconds for `steps` decode steps of the reference algorithm over `lengths` rows.
+
+    Follows kv_cache.py (staged append with full re-validation on every
+    call), dense.apply_rope and attention.paged_attention's page loop, via the
+    oracle restatement, on a pool of `num_blocks` blocks.
+    """
+    from oracle import attention as oracle_attention
+    from oracle import kv_write, rope
+    from oracle.allocator import OracleAllocator
+    from pagedcore_b200 import workloads
+
+    table = rope.cos_sin_table()
+    allocator = OracleAllocator(num_blocks, audit=True)
+    pool = np.empty((22, 2, num_blocks, 16, 4, 64), dtype=np.float16)
+    pattern = workloads.normal_f16(workloads.rng(seed, 9), (22, 16, 4, 64))
+    rows = list(range(len(lengths)))
+    for row, length in zip(rows, lengths):
+        allocator.create(row, workloads.blocks_for(length + steps + warmup))
+        slots = np.asarray(allocator.append(row, length))
+        for start in range(0, length, 16):
+            part = slots[start : start + 16]
+            kv_write.write_rows(pool, 0, pattern[:, : len(part)], pattern[:, : len(part)], part)
+    q, k, v = workloads.decode_step_inputs(seed, len(rows), 0)
+    elapsed = 0.0
+    for step in range(warmup + steps):
+        begin = time.perf_counter()
+        slots, positions = allocator.decode_begin(tuple(rows))
+        slots, positions = np.asarray(slots), np.asarray(positions)
+        for layer in range(LAYERS):
+            q_rot = rope.rotate(q[layer][None], positions, table)[0]
+            kv_write.append_rotated(pool, k[layer][None], v[layer][None], slots, positions, table, layer_begin=layer)
+            for row in rows:
+                blocks, length = allocator.view(row)
+                oracle_attention.paged_attention(pool, layer, q_rot[row], blocks, length)
+        allocator.decode_commit()
+        if step >= warmup:
+            elapsed += time.perf_counter() - begin
+    return elapsed
+
+
+def _reference_worker(args: tuple) -> float:
+    lengths, num_blocks, steps, warmup, seed = args
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(1):
+        return oracle_decode_rows(lengths, num_blocks, steps, warmup, seed)
+
+
+def run_reference_arm(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+
+    from pagedcore_b200 import workloads
+
+    cores = os.cpu_count() or 1
+    case = workloads.decode_case(seed=4, batch=SEQUENCES, steps=args.warmup + args.steps)
+    # A bounded sample of the workload: `sample` rows of the rank-0 batch, one
+    # row per process, all host cores busy.
+    sample = min(SEQUENCES, max(cores, 8))
+    lengths = [int(n) for n in case.lengths[:sample]]
+    per_worker = [[n] for n in lengths]
+    ctx = mp.get_context("spawn")
+    start = time.perf_counter()
+    with ctx.Pool(processes=min(cores, sample)) as pool:
+        times = pool.map(_reference_worker, [(rows, case.num_blocks, args.steps, args.warmup, 4 + i)
+                                             for i, rows in enumerate(per_worker)])
+    wall = time.perf_counter() - start
+    busiest = max(times)
+    tokens = sample * args.steps
+    value = tokens / busiest
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * busiest / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded)",
+        "config": _config(args.gpus),
+        "cpu_baseline": {
+            "value": value,
+            "unit": "tokens/s",
+            "cores": min(cores, sample),
+            "kind": "port",
+            "sample": f"{sample} of {SEQUENCES} rows (one per process), {args.steps} timed decode steps x 22 layers, "
+                      f"oracle restatement of the reference CPU path, full ledger re-validation per call; "
+                      f"wall {wall:.1f}s incl. setup",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU path.
+# ---------------------------------------------------------------------------
+def _config(n_gpus: int) -> dict:
+    return {
+        "workload": "BASELINE config 4, KV hot path: 256 sequences per GPU, contexts U[1, 1984], churned "
+                    "block tables; one step = staged append + 22 x (fused K/Q-RoPE KV scatter, split-K GQA "
+                    "decode attention + combine) + commit; dense GEMMs not included",
+        "sequences_per_gpu": SEQUENCES,
+        "layers": LAYERS,
+        "heads": "32 query / 4 KV, head_dim 64, block 16",
+        "l2": "inputs larger than L2: each attention launch streams ~0.25 GB of K/V (L2 is 126 MB)",
+        "parallelism": f"dp{n_gpus} (independent sequences, one KV pool per GPU, no collective)",
+    }
+
+
+def _peak_hbm() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _traffic_per_launch() -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "decode_attention_cfg4.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices: list[int]) -> None:
+        self.devices = devices
+        self.proc = None
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(d) for d in self.devices)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.output, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.output, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        clocks, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.output or "").splitlines():
+            fields = [f.strip() for f in line.split(",")]
+            if len(fields) < 9:
+                continue
+            try:
+                clocks.append(float(fields[1]))
+                maxes.append(float(fields[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, fields[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(clocks) if clocks else None,
+            "sm_max_mhz": max(maxes) if maxes else None,
+            "samples": len(clocks),
+            "reasons": sorted(reasons),
+        }
+
+
+def run_gpu_arm(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    from pagedcore_b200 import workloads
+    from pagedcore_b200.attention import paged_decode_attention
+    from pagedcore_b200.engine_types import KVReservation, RequestId
+    from pagedcore_b200.kv_cache import KVAllocator
+
+    total_steps = args.warmup + args.steps
+    seed = 4 + 1000 * rank
+    case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=2 * total_steps)
+    pool = torch.empty((22, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
+    allocator = KVAllocator(pool, validation="incremental")
+
+    # Fragment the free list with seeded churn, then prefill the batch.
+    generator = torch.Generator(device=device).manual_seed(seed)
+    zero = torch.zeros(22, 64, 4, 64, dtype=torch.float16, device=device)
+    for op in case.churn:
+        rid = RequestId(f"churn{op.request}")
+        if op.kind == "create":
+            allocator.create(KVReservation(rid, op.credits))
+            allocator.append(rid, zero[:, : op.tokens], zero[:, : op.tokens])
+        else:
+            allocator.release_all(rid)
+    requests = tuple(RequestId(f"seq{i}") for i in range(SEQUENCES))
+    for request, length, credits in zip(requests, case.lengths.tolist(), case.credits.tolist()):
+        allocator.create(KVReservation(request, credits))
+        key = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+        value = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+        allocator.append(request, key, value, rotate=True)
+    torch.cuda.synchronize(device)
+
+    def inputs(index: int) -> tuple[torch.Tensor, ...]:
+        g = torch.Generator(device=device).manual_seed(seed * 7919 + index)
+        q = torch.randn(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device, generator=g)
+        k = torch.randn(22, SEQUENCES, 4, 64, dtype=torch.float16, device=device, generator=g)
+        v = torch.randn(22, SEQUENCES, 4, 64, dtype=torch.float16, device=device, generator=g)
+        return q, k, v
+
+    device_inputs = [inputs(i) for i in range(2)]
+    out = torch.empty(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(q, k, v, attn_events=None) -> None:
+        with allocator.append_decode(requests):
+            for layer in range(LAYERS):
+                q_rot = allocator.write_decode_batch(layer, k[layer], v[layer], query=q[layer], rotate=True)
+                if attn_events is not None:
+                    attn_events[layer][0].record(stream)
+                paged_decode_attention(q_rot, allocator, requests, layer_index=layer, out=out[layer])
+                if attn_events is not None:
+                    attn_events[layer][1].record(stream)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    for i in range(args.warmup):
+        step(*device_inputs[i % 2])
+    allocator.check_device_errors()
+
+    # Attention-kernel algorithmic bytes per step, from the plan of the step's batch.
+    def attention_bytes() -> tuple[float, int]:
+        with allocator.append_decode(requests):
+            batch = None
+            for layer in range(LAYERS):
+                allocator.write_decode_batch(layer, device_inputs[0][1][layer], device_inputs[0][2][layer])
+                if layer == 0:
+                    batch = allocator.decode_batch(requests, layer_index=0)
+            lengths = batch.host_lengths.astype(np.int64)
+            plan = batch.plan
+            prefix = np.concatenate([[0], np.cumsum((lengths + 15) // 16)])
+            first = prefix[:-1] // plan.blocks_per_cta
+            last = (prefix[1:] - 1) // plan.blocks_per_cta
+            segments = last - first + 1
+            split = segments > 1
+            per_row = 1024 * lengths + 4 * ((lengths + 15) // 16) + 32 * 64 * 2 * 2 + 4 * 2
+            per_row = per_row + np.where(split, segments * 32 * 66 * 4 * 2, 0)
+            launches = 2 if plan.grid > 1 else 1
+            return float(per_row.sum()), launches
+
+    # One extra staged step (its tokens are real appends) measures the plan.
+    attn_bytes_per_launch, kernels_per_attention = attention_bytes()
+
+    attn_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
+                   for _ in range(args.steps)]
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler([local_rank]) as clocks:
+        torch.cuda.nvtx.range_push("timed")
+        start.record(stream)
+        for i in range(args.steps):
+            step(*device_inputs[i % 2], attn_events[i])
+        end.record(stream)
+        torch.cuda.nvtx.range_pop()
+        barrier()
+    elapsed_ms = start.elapsed_time(end)
+    attn_ms = sum(a.elapsed_time(b) for per_step in attn_events for a, b in per_step)
+    allocator.check_device_errors()
+
+    # End to end through the public API with host buffers.
+    host_inputs = [tuple(t.cpu().pin_memory() for t in device_inputs[i]) for i in range(2)]
+    staging = [torch.empty_like(t) for t in device_inputs[0]]
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs[0])
+    d2h_bytes = host_out.numel() * host_out.element_size()
+    for i in range(2):
+        for dst, src in zip(staging, host_inputs[i]):
+            dst.copy_(src, non_blocking=True)
+        step(*staging)
+        host_out.copy_(out, non_blocking=True)
+    barrier()
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_start.record(stream)
+    for i in range(args.steps):
+        for dst, src in zip(staging, host_inputs[i % 2]):
+            dst.copy_(src, non_blocking=True)
+        step(*staging)
+        host_out.copy_(out, non_blocking=True)
+    e2e_end.record(stream)
+    barrier()
+    e2e_ms = e2e_start.elapsed_time(e2e_end)
+    allocator.check_device_errors()
+
+    times = torch.tensor([elapsed_ms, e2e_ms, attn_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms, attn_ms = times.tolist()
+
+    if rank == 0:
+        tokens = world * SEQUENCES * args.steps
+        value = tokens / (elapsed_ms / 1000.0)
+        peak, peak_kind = _peak_hbm()
+        launch_ms = attn_ms / (args.steps * LAYERS)
+        achieved = attn_bytes_per_launch / (launch_ms / 1000.0) / 1e9
+        traffic = _traffic_per_launch()
+        launches_per_step = LAYERS * (1 + kernels_per_attention)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded K/V/Q ~N(0,1), contexts U[1, 1984]); the reference publishes no inputs",
+            "config": _config(world),
+            "attn_hbm_gbs": achieved,
+            "attn_frac_of_peak": achieved / peak,
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "decode attention (split-K kernel + combine kernel), per layer launch",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "algorithmic_bytes_per_launch": attn_bytes_per_launch,
+                "avg_launch_ms": launch_ms,
+                "traffic": traffic,
+            },
+            "e2e": {
+                "value": tokens / (e2e_ms / 1000.0),
+                "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d_bytes,
+                "d2h_bytes_per_step": d2h_bytes,
+                "path": "pinned host Q/K/V -> device, KVAllocator.write_decode_batch + paged_decode_attention, "
+                        "attention outputs -> pinned host, every step",
+            },
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            sample_rows = [int(n) for n in case.lengths[:4]]
+            seconds = oracle_decode_rows(sample_rows, case.num_blocks, steps=2, warmup=0, seed=seed)
+            line["cpu_baseline"] = {
+                "value": len(sample_rows) * 2 / seconds,
+                "unit": "tokens/s",
+                "cores": 1,
+                "kind": "port",
+                "sample": f"{len(sample_rows)} rows x 2 decode steps x 22 layers of the same workload, single "
+                          f"thread, oracle restatement of the reference CPU path ({seconds:.1f}s)",
+            }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--sequences", type=int, default=SEQUENCES,
+                        help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
+    args = parser.parse_args()
+    globals()["SEQUENCES"] = args.sequences
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

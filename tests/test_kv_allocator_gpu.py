@@ -353,9 +353,9 @@ def test_failed_write_launch_preserves_state_and_allows_retry(monkeypatch: pytes
 
 def test_oracle_and_kernel_agree_on_random_prefill_positions(rope_golden: np.ndarray) -> None:
     device = cuda_device()
-    allocator = KVAllocator(nan_pool(300, device))
-    oracle_pool = kv_write.new_pool(300)
-    oracle = OracleAllocator(300, audit=False)
+    allocator = KVAllocator(nan_pool(1000, device))
+    oracle_pool = kv_write.new_pool(1000)
+    oracle = OracleAllocator(1000, audit=False)
     generator = workloads.rng(5, 1)
     for request in range(12):
         first = int(generator.integers(1, 600))
