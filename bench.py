@@ -152,8 +152,8 @@ def run_reference_arm(args: argparse.Namespace) -> None:
 def _config(n_gpus: int) -> dict:
     return {
         "workload": "BASELINE config 4, KV hot path: 256 sequences per GPU, contexts U[1, 1984], churned "
-                    "block tables; one step = staged append + 22 x (fused K/Q-RoPE KV scatter, split-K GQA "
-                    "decode attention + combine) + commit; dense GEMMs not included",
+                    "block tables; one step = staged append + 22 fused decode-layer launches (Q/K RoPE, "
+                    "new-token KV write, split-K GQA decode attention) + commit; dense GEMMs not included",
         "sequences_per_gpu": SEQUENCES,
         "layers": LAYERS,
         "heads": "32 query / 4 KV, head_dim 64, block 16",
@@ -297,10 +297,9 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     def step(q, k, v, attn_events=None) -> None:
         with allocator.append_decode(requests):
             for layer in range(LAYERS):
-                q_rot = allocator.write_decode_batch(layer, k[layer], v[layer], query=q[layer], rotate=True)
                 if attn_events is not None:
                     attn_events[layer][0].record(stream)
-                paged_decode_attention(q_rot, allocator, requests, layer_index=layer, out=out[layer])
+                allocator.decode_layer(layer, q[layer], k[layer], v[layer], out=out[layer])
                 if attn_events is not None:
                     attn_events[layer][1].record(stream)
 
@@ -313,28 +312,28 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         step(*device_inputs[i % 2])
     allocator.check_device_errors()
 
-    # Attention-kernel algorithmic bytes per step, from the plan of the step's batch.
-    def attention_bytes() -> tuple[float, int]:
+    # Algorithmic bytes of one fused decode-layer launch, from the plan of the
+    # staged batch: K/V streamed (1024 B per cached token, the new one
+    # included), block-table entries, Q in / attention out (4 KiB each), the
+    # new token's K/V in (1 KiB) and written to the pool (1 KiB), lengths and
+    # prefix, and the split partials written then read back (32 heads x 66 FP32
+    # per segment of a split row).
+    def layer_bytes() -> float:
         with allocator.append_decode(requests):
-            batch = None
+            batch = allocator.staged_decode_batch()
             for layer in range(LAYERS):
-                allocator.write_decode_batch(layer, device_inputs[0][1][layer], device_inputs[0][2][layer])
-                if layer == 0:
-                    batch = allocator.decode_batch(requests, layer_index=0)
-            lengths = batch.host_lengths.astype(np.int64)
-            plan = batch.plan
-            prefix = np.concatenate([[0], np.cumsum((lengths + 15) // 16)])
-            first = prefix[:-1] // plan.blocks_per_cta
-            last = (prefix[1:] - 1) // plan.blocks_per_cta
-            segments = last - first + 1
-            split = segments > 1
-            per_row = 1024 * lengths + 4 * ((lengths + 15) // 16) + 32 * 64 * 2 * 2 + 4 * 2
-            per_row = per_row + np.where(split, segments * 32 * 66 * 4 * 2, 0)
-            launches = 2 if plan.grid > 1 else 1
-            return float(per_row.sum()), launches
+                allocator.decode_layer(layer, *(x[layer] for x in device_inputs[0]), out=out[layer])
+        lengths = batch.host_lengths.astype(np.int64)
+        plan = batch.plan
+        blocks = (lengths + 15) // 16
+        prefix = np.concatenate([[0], np.cumsum(blocks)])
+        segments = (prefix[1:] - 1) // plan.blocks_per_cta - prefix[:-1] // plan.blocks_per_cta + 1
+        per_row = 1024 * lengths + 4 * blocks + 2 * 4096 + 2 * 1024 + 8
+        per_row = per_row + np.where(segments > 1, segments * 32 * 66 * 4 * 2, 0)
+        return float(per_row.sum())
 
     # One extra staged step (its tokens are real appends) measures the plan.
-    attn_bytes_per_launch, kernels_per_attention = attention_bytes()
+    layer_bytes_per_launch = layer_bytes()
 
     attn_events = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
                    for _ in range(args.steps)]
@@ -349,7 +348,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         torch.cuda.nvtx.range_pop()
         barrier()
     elapsed_ms = start.elapsed_time(end)
-    attn_ms = sum(a.elapsed_time(b) for per_step in attn_events for a, b in per_step)
+    layer_ms = sum(a.elapsed_time(b) for per_step in attn_events for a, b in per_step)
     allocator.check_device_errors()
 
     # End to end through the public API with host buffers.
@@ -376,19 +375,19 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     e2e_ms = e2e_start.elapsed_time(e2e_end)
     allocator.check_device_errors()
 
-    times = torch.tensor([elapsed_ms, e2e_ms, attn_ms], dtype=torch.float64, device=device)
+    times = torch.tensor([elapsed_ms, e2e_ms, layer_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, attn_ms = times.tolist()
+    elapsed_ms, e2e_ms, layer_ms = times.tolist()
 
     if rank == 0:
         tokens = world * SEQUENCES * args.steps
         value = tokens / (elapsed_ms / 1000.0)
         peak, peak_kind = _peak_hbm()
-        launch_ms = attn_ms / (args.steps * LAYERS)
-        achieved = attn_bytes_per_launch / (launch_ms / 1000.0) / 1e9
+        launch_ms = layer_ms / (args.steps * LAYERS)
+        achieved = layer_bytes_per_launch / (launch_ms / 1000.0) / 1e9
         traffic = _traffic_per_launch()
-        launches_per_step = LAYERS * (1 + kernels_per_attention)
+        launches_per_step = LAYERS
         line = {
             "metric": METRIC,
             "value": value,
@@ -407,13 +406,14 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             "attn_frac_of_peak": achieved / peak,
             "roofline": {
                 "bound": "hbm",
-                "kernel": "decode attention (split-K kernel + combine kernel), per layer launch",
+                "kernel": "fused decode layer (decode_kernel<6,true>: Q/K RoPE, new-token KV write, split-K "
+                          "GQA attention, in-kernel merge), one launch per layer",
                 "achieved": achieved,
                 "peak": peak,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "algorithmic_bytes_per_launch": attn_bytes_per_launch,
+                "algorithmic_bytes_per_launch": layer_bytes_per_launch,
                 "avg_launch_ms": launch_ms,
                 "traffic": traffic,
             },

@@ -124,7 +124,11 @@ int pkv_ledger_view(pkv_ledger *ledger, int64_t request, int32_t layer, int32_t 
 /* Device-ready metadata for a batch at `layer` (the batched form of
  * iter_layer_blocks): lengths[count], prefix[count+1] (cumulative block
  * counts) and the flat concatenation of the tables, flat[prefix[b] + j] =
- * physical block of logical block j of row b.  flat_capacity bounds flat. */
+ * physical block of logical block j of row b.  flat_capacity bounds flat.
+ * layer == PKV_VIEW_STAGED gives every staged row's staged view (length + 1,
+ * new block included) whatever layers were written: the view of a caller
+ * that writes the new token in the same launch (pkv_decode_layer). */
+#define PKV_VIEW_STAGED (-2)
 int pkv_ledger_batch(pkv_ledger *ledger, const int64_t *requests, int32_t count, int32_t layer,
                      int32_t *out_lengths, int32_t *out_prefix, int32_t *out_flat,
                      int32_t flat_capacity, int32_t *out_total_blocks);
@@ -194,6 +198,26 @@ int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, co
                          const int32_t *flat, int32_t batch, int32_t total_blocks, int32_t grid,
                          int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
                          int64_t workspace_bytes, int32_t *error_flag, void *stream);
+
+/* One decode layer for a staged batch in one launch: the fused form of
+ * write_decode_layer (kv_cache.py:221-246) + apply_rope on Q and K
+ * (dense.py:33-61) + paged_attention (attention.py:14-53).  For every row b:
+ * the new token sits at position lengths[b]-1 (lengths/prefix/flat from
+ * pkv_ledger_batch with PKV_VIEW_STAGED); its K (rotated) and V are written
+ * to its pool slot at `layer`, Q is rotated at the same position, and the
+ * attention over all lengths[b] tokens is written to out.  query: unrotated
+ * FP16 [batch][32][64] (rows query_stride apart); key/value: FP16
+ * [batch][4][64] (rows kv_stride apart); rope_table as for pkv_append_kv.
+ * Split rows are merged inside the launch: counters is an int32 [batch][4]
+ * device array that must be zero before the first call; the kernel leaves it
+ * zero again (reset it after a device error).  Same plan and workspace as
+ * pkv_decode_attention. */
+int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
+                     const void *key, const void *value, int64_t kv_stride, const void *rope_table,
+                     const int32_t *lengths, const int32_t *prefix, const int32_t *flat, int32_t batch,
+                     int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
+                     void *workspace, int64_t workspace_bytes, int32_t *counters, int32_t *error_flag,
+                     void *stream);
 
 #ifdef __cplusplus
 }

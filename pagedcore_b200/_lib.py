@@ -21,6 +21,7 @@ PKV_CUDA_ERROR = 4
 
 VALIDATE_INCREMENTAL = 0
 VALIDATE_FULL = 1
+VIEW_STAGED = -2
 
 DEVICE_BAD_BLOCK = 1
 DEVICE_BAD_POSITION = 2
@@ -86,6 +87,34 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ],
     ),
     "pkv_decode_plan": (c_int, [c_int32, c_int32, c_int32, i32p, i32p, i64p]),
+    "pkv_decode_layer": (
+        c_int,
+        [
+            c_void_p,  # pool
+            c_int32,  # num_blocks
+            c_int32,  # layer
+            c_void_p,  # query
+            c_int64,  # query_stride
+            c_void_p,  # key
+            c_void_p,  # value
+            c_int64,  # kv_stride
+            c_void_p,  # rope_table
+            c_void_p,  # lengths
+            c_void_p,  # prefix
+            c_void_p,  # flat
+            c_int32,  # batch
+            c_int32,  # total_blocks
+            c_int32,  # grid
+            c_int32,  # blocks_per_cta
+            c_void_p,  # out
+            c_int64,  # out_stride
+            c_void_p,  # workspace
+            c_int64,  # workspace_bytes
+            c_void_p,  # counters
+            c_void_p,  # error_flag
+            c_void_p,  # stream
+        ],
+    ),
     "pkv_decode_attention": (
         c_int,
         [

@@ -3,38 +3,49 @@
 // Replaces PagedCore's paged_attention (src/pagedcore/attention.py:14-53),
 // which for one request and one layer computes, in FP32 from FP16 pages,
 //   o[h] = sum_t softmax_t(q[h] . k[t, h/8] * 0.125) v[t, h/8]
-// and rounds once to FP16.  Here a whole batch of requests is served by two
-// launches:
+// and rounds once to FP16.  A whole batch of requests is served at once.
 //
-// 1. decode_attention_kernel - balanced split-K over the batch's 16-token
-//    blocks.  The batch's block tables are concatenated into one flat list
-//    (flat[prefix[b] + j] = physical block of logical block j of row b); CTA
-//    g owns the contiguous global block range [g*W, (g+1)*W), which may cover
-//    the tail of one row, whole short rows and the head of another.  Every
-//    CTA therefore streams the same number of KV bytes whatever the ragged
-//    lengths.  Warp w of a CTA serves KV head w and its 8 query heads (GQA).
-//    Each warp runs its own TMA pipeline: per block, two 2 KiB boxes (the 16
-//    K rows and 16 V rows of its head, 128 B each) land in shared memory with
-//    the 128-byte swizzle, so ldmatrix reads are bank-conflict free.
-//    Tensor-core tiles (mma.sync m16n8k16, FP16 in, FP32 accumulate):
-//      S^T[16 tok x 8 heads] = K[16 x 64] . Q^T[64 x 8]        (4 MMAs)
-//      O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]     (4 MMAs)
-//    so the 8-head GQA group fills the N=8 side exactly.  The S^T accumulator
-//    becomes the P^T operand with two movmatrix transposes.  Softmax is the
-//    online (running max) form in base 2 with FP32 state.  P is rounded to
-//    FP16 for the PV MMA after scaling by 2^15 (p = 2^(s - m + 15) <= 2^15),
-//    which keeps weights down to ~2^-24 of the row maximum representable as
-//    normal FP16 numbers; the normaliser l sums the same rounded weights.
-//    A row fully inside one CTA is normalised and written as FP16 directly;
-//    a row split across CTAs leaves (m, l, O) partials in the workspace at
-//    index row + cta (unique: along the CTA order the (row, cta) pairs form a
-//    monotone staircase, so row + cta strictly increases).
-// 2. decode_combine_kernel - merges the partials of split rows.
+// Work split - balanced split-K over the batch's 16-token blocks.  The batch's
+// block tables are concatenated into one flat list (flat[prefix[b] + j] =
+// physical block of logical block j of row b); CTA g owns the contiguous
+// global block range [g*W, (g+1)*W), which may cover the tail of one row,
+// whole short rows and the head of another, so every CTA streams the same
+// number of KV bytes whatever the ragged lengths.  Warp w of a CTA serves KV
+// head w and its 8 query heads (GQA).
 //
-// The pass is HBM-bound: per (row, layer) it reads 1024*L bytes of K/V.
-// Unwritten slots of a row's last block may hold anything (the reference
-// pool is uninitialised, tests fill it with NaN): their scores are masked to
-// -inf and their V rows are zeroed in shared memory before the PV MMA.
+// Data movement - each warp runs its own TMA pipeline of STAGES stages: per
+// block, two 2 KiB boxes (the 16 K rows and 16 V rows of its head, 128 B
+// each, 512 B apart in the pool) land in shared memory with the 128-byte
+// swizzle, so ldmatrix reads are bank-conflict free.  Waits are bounded.
+//
+// Math - tensor-core tiles (mma.sync m16n8k16, FP16 in, FP32 accumulate):
+//   S^T[16 tok x 8 heads]  = K[16 x 64] . Q^T[64 x 8]         (4 MMAs)
+//   O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]      (4 MMAs)
+// so the 8-head GQA group fills the N=8 side exactly; the S^T accumulator
+// becomes the P^T operand with two movmatrix transposes.  Softmax is the
+// online (running max) form in base 2 with FP32 state.  P is rounded to FP16
+// for the PV MMA after scaling by 2^15 (p = 2^(s - m + 15) <= 2^15), which
+// keeps weights down to ~2^-24 of the row maximum as normal FP16 numbers; the
+// normaliser l sums the same rounded weights.  Unwritten slots of a row's
+// last block may hold anything (the pool is uninitialised; tests fill it with
+// NaN): their scores are masked to -inf and their V rows are zeroed in shared
+// memory before the PV MMA.
+//
+// Split rows - a row inside one CTA is normalised and written as FP16
+// directly.  A row split across CTAs leaves (m, l, O) partials at index
+// row + cta (unique: along the CTA order the (row, cta) pairs form a
+// monotone staircase, so row + cta strictly increases).  Two variants merge
+// them:
+//   * two-pass (paged_attention's drop-in path): decode_combine_kernel runs
+//     after the split kernel;
+//   * fused decode layer: the last warp to finish a (row, KV head) - counted
+//     with one atomic per warp, no waiting - merges the partials itself.
+//
+// The fused decode-layer variant also does the layer's KV append: it applies
+// RoPE to Q (every CTA of the row, in registers) and to the new token's K
+// (bit-exact with dense.py:48-59), writes K and V of the new token to the
+// pool slot (kv_cache.py:244-245) and patches that slot of the staged tile in
+// shared memory, so attention sees the token in the same launch.
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -57,6 +68,7 @@ constexpr int kKvHeads = PKV_KV_HEADS;
 constexpr int kQueryHeads = PKV_QUERY_HEADS;
 constexpr int kGroup = kQueryHeads / kKvHeads;  // 8 query heads per KV head
 constexpr int kBlockTokens = PKV_BLOCK_TOKENS;
+constexpr int kRopeHalf = kHeadDim / 2;
 constexpr int kRowBytes = kHeadDim * 2;                  // 128 B: one head of one token
 constexpr int kTileBytes = kBlockTokens * kRowBytes;     // 2 KiB: one head of one block
 constexpr int kStageBytes = 2 * kTileBytes;              // K tile + V tile
@@ -73,6 +85,31 @@ constexpr int smem_bytes() {
     return kWarps * STAGES * kStageBytes + 1024;  // + alignment slack
 }
 
+struct LayerArgs {
+    const __half *query;       // [B][32][64], rows query_stride apart (rotated unless FUSED)
+    int64_t query_stride;
+    const __half *key_new;     // FUSED: new token's unrotated K [B][4][64]
+    const __half *value_new;   // FUSED: new token's V [B][4][64]
+    int64_t new_stride;        // elements between rows of key_new / value_new
+    const __half *rope_cos;    // FUSED: FP16 [2048][32]
+    const __half *rope_sin;
+    __half *pool;              // FUSED: pool base, for the new token's K/V
+    const int32_t *lengths;    // [B]
+    const int32_t *prefix;     // [B+1]
+    const int32_t *flat;       // [total_blocks]
+    int32_t batch;
+    int32_t total_blocks;
+    int32_t blocks_per_cta;
+    int32_t num_blocks;
+    int32_t layer;
+    __half *out;               // [B][32][64], rows out_stride apart
+    int64_t out_stride;
+    float *part_o;             // [(B + grid)][32][64]
+    float *part_ml;            // [(B + grid)][32][2]
+    int32_t *counters;         // FUSED: [B][4], zero between launches
+    int32_t *error_flag;
+};
+
 __device__ __forceinline__ float warp_max8(float v) {
     // Reduce over the 8 lanes that share lane % 4 (the token rows of a fragment).
     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
@@ -87,6 +124,27 @@ __device__ __forceinline__ float warp_sum8(float v) {
     v += __shfl_xor_sync(0xffffffffu, v, 16);
     return v;
 }
+
+// One FP16 RoPE step, as the reference's eager ops round it:
+// fp16(fp16(x * c) + fp16(r * s)) with r = -rot or rot, on a half2 pair.
+__device__ __forceinline__ uint32_t rope_half2(uint32_t x, uint32_t rot, bool negate, uint32_t c, uint32_t s) {
+    const float2 xf = __half22float2(*reinterpret_cast<const __half2 *>(&x));
+    float2 rf = __half22float2(*reinterpret_cast<const __half2 *>(&rot));
+    const float2 cf = __half22float2(*reinterpret_cast<const __half2 *>(&c));
+    const float2 sf = __half22float2(*reinterpret_cast<const __half2 *>(&s));
+    if (negate) {
+        rf.x = -rf.x;
+        rf.y = -rf.y;
+    }
+    const float a0 = __half2float(__float2half_rn(xf.x * cf.x));
+    const float a1 = __half2float(__float2half_rn(xf.y * cf.y));
+    const float b0 = __half2float(__float2half_rn(rf.x * sf.x));
+    const float b1 = __half2float(__float2half_rn(rf.y * sf.y));
+    __half2 r = __halves2half2(__float2half_rn(a0 + b0), __float2half_rn(a1 + b1));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+__device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
 // Fetch one block's K and V boxes of KV head `head` into a pipeline stage
 // (called by one lane).  An out-of-range block id sets the error flag and
@@ -104,18 +162,14 @@ __device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t bloc
     pkv::tma_load_3d(dst + kTileBytes, map, 0, head, v_rows + block * kBlockTokens, bar);
 }
 
-template <int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
-    const __grid_constant__ CUtensorMap pool_map, const __half *__restrict__ query,
-    int64_t query_stride, const int32_t *__restrict__ lengths, const int32_t *__restrict__ prefix,
-    const int32_t *__restrict__ flat, int32_t batch, int32_t total_blocks, int32_t blocks_per_cta,
-    int32_t num_blocks, int32_t layer, __half *__restrict__ out, int64_t out_stride,
-    float *__restrict__ part_o, float *__restrict__ part_ml, int32_t *__restrict__ error_flag) {
+template <int STAGES, bool FUSED>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ LayerArgs a) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
 
-    const int begin = blockIdx.x * blocks_per_cta;
-    const int end = min(begin + blocks_per_cta, total_blocks);
+    const int begin = blockIdx.x * a.blocks_per_cta;
+    const int end = min(begin + a.blocks_per_cta, a.total_blocks);
     if (begin >= end) return;
 
     const int warp = threadIdx.x >> 5;
@@ -124,7 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
     const int t = lane & 3;   // fragment column pair
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const uint32_t tiles = pkv::smem_addr(smem + warp * STAGES * kStageBytes);
+    uint8_t *warp_tiles = smem + warp * STAGES * kStageBytes;
+    const uint32_t tiles = pkv::smem_addr(warp_tiles);
     const uint32_t bar0 = pkv::smem_addr(&barriers[warp * kMaxStages]);
 
     if (lane == 0) {
@@ -135,43 +190,94 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
 
     // Rows of this head's K and V boxes in the 3-D view of the pool
     // (dim 64, kv head 4, pool row = ((layer*2 + kv)*num_blocks + block)*16).
-    const int32_t k_rows = (layer * 2 + 0) * num_blocks * kBlockTokens;
-    const int32_t v_rows = (layer * 2 + 1) * num_blocks * kBlockTokens;
+    const int32_t k_rows = (a.layer * 2 + 0) * a.num_blocks * kBlockTokens;
+    const int32_t v_rows = (a.layer * 2 + 1) * a.num_blocks * kBlockTokens;
 
     // Producer state (used by lane 0 only): the next global block to fetch.
     int next_fetch = begin;
     if (lane == 0) {
         const int n = min(STAGES, end - begin);
         for (int s = 0; s < n; ++s) {
-            issue_block(&pool_map, flat[next_fetch], num_blocks, k_rows, v_rows, warp,
-                        tiles + s * kStageBytes, bar0 + 8 * s, error_flag);
+            issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp,
+                        tiles + s * kStageBytes, bar0 + 8 * s, a.error_flag);
             ++next_fetch;
         }
     }
 
     // First row of the range: the largest b with prefix[b] <= begin.
-    int lo = 0, hi = batch - 1;
+    int lo = 0, hi = a.batch - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (prefix[mid] <= begin) lo = mid; else hi = mid - 1;
+        if (a.prefix[mid] <= begin) lo = mid; else hi = mid - 1;
     }
 
     int consumed = 0;
     bool failed = false;
     for (int row = lo, i = begin; i < end; ++row) {
-        const int row_first = prefix[row];
-        const int row_last = prefix[row + 1];
+        const int row_first = a.prefix[row];
+        const int row_last = a.prefix[row + 1];
         const int seg_end = min(end, row_last);
-        const int length = lengths[row];
+        const int length = a.lengths[row];
 
-        // Q^T fragments (B operand) of this warp's 8 query heads.
-        const __half *q = query + row * query_stride + (warp * kGroup + g) * kHeadDim;
+        // Q^T fragments (B operand) of this warp's 8 query heads: lane holds
+        // dims 16ks + 2t + {0,1} and 16ks + 8 + 2t + {0,1} of head 8*warp + g.
+        const __half *q = a.query + row * a.query_stride + (warp * kGroup + g) * kHeadDim;
         uint32_t qf[4][2];
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-            qf[ks][0] = *reinterpret_cast<const uint32_t *>(q + 16 * ks + 2 * t);
-            qf[ks][1] = *reinterpret_cast<const uint32_t *>(q + 16 * ks + 8 + 2 * t);
+            qf[ks][0] = ld32(q + 16 * ks + 2 * t);
+            qf[ks][1] = ld32(q + 16 * ks + 8 + 2 * t);
         }
+
+        // Fused append: the new token sits at position length-1 of the row.
+        uint32_t new_k = 0, new_v = 0;
+        int new_slot = -1;
+        if constexpr (FUSED) {
+            int pos = length - 1;
+            if (pos < 0 || pos >= PKV_CONTEXT_LIMIT) {
+                if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_POSITION);
+                pos = 0;
+            }
+            // RoPE of Q in registers: dims d < 32 pair with d + 32 (k-step ks + 2).
+            const __half *cs = a.rope_cos + pos * kRopeHalf;
+            const __half *sn = a.rope_sin + pos * kRopeHalf;
+            uint32_t rq[4][2];
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int d = (16 * ks + 8 * h + 2 * t) & (kRopeHalf - 1);
+                    rq[ks][h] = rope_half2(qf[ks][h], qf[ks ^ 2][h], ks < 2, ld32(cs + d), ld32(sn + d));
+                }
+            }
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                qf[ks][0] = rq[ks][0];
+                qf[ks][1] = rq[ks][1];
+            }
+            if (seg_end == row_last) {
+                // This CTA holds the row's last block: rotate the new K (lane owns
+                // dims 2*lane, 2*lane+1 of head `warp`) and write K/V to the pool.
+                const __half *kn = a.key_new + row * a.new_stride + warp * kHeadDim;
+                const __half *vn = a.value_new + row * a.new_stride + warp * kHeadDim;
+                const int d = 2 * lane;
+                new_k = rope_half2(ld32(kn + d), ld32(kn + ((d + kRopeHalf) & (kHeadDim - 1))), d < kRopeHalf,
+                                   ld32(cs + (d & (kRopeHalf - 1))), ld32(sn + (d & (kRopeHalf - 1))));
+                new_v = ld32(vn + d);
+                new_slot = pos & (kBlockTokens - 1);
+                const int32_t block = a.flat[row_last - 1];
+                if (block >= 0 && block < a.num_blocks) {
+                    const int64_t base =
+                        (((static_cast<int64_t>(a.layer) * 2) * a.num_blocks + block) * kBlockTokens + new_slot) *
+                            (kKvHeads * kHeadDim) +
+                        warp * kHeadDim + d;
+                    const int64_t v_offset = static_cast<int64_t>(a.num_blocks) * kBlockTokens * kKvHeads * kHeadDim;
+                    *reinterpret_cast<uint32_t *>(a.pool + base) = new_k;
+                    *reinterpret_cast<uint32_t *>(a.pool + base + v_offset) = new_v;
+                }
+            }
+        }
+
         float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
         float o[4][4];
 #pragma unroll
@@ -187,15 +293,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
             const uint32_t ktile = tiles + stage * kStageBytes;
             const uint32_t vtile = ktile + kTileBytes;
             const int valid = min(kBlockTokens, length - (i - row_first) * kBlockTokens);
+            uint8_t *stage_tiles = warp_tiles + stage * kStageBytes;
             if (valid < kBlockTokens) {
                 // Zero the V rows of unwritten slots: P is 0 there, but 0 * NaN is NaN.
-                uint8_t *vrows = smem + warp * STAGES * kStageBytes + stage * kStageBytes + kTileBytes;
+                uint8_t *vrows = stage_tiles + kTileBytes;
                 for (int idx = lane; idx < (kBlockTokens - valid) * 8; idx += 32) {
                     *reinterpret_cast<uint4 *>(vrows + (valid + idx / 8) * kRowBytes + (idx % 8) * 16) =
                         make_uint4(0, 0, 0, 0);
                 }
-                __syncwarp();
             }
+            if (FUSED && new_slot >= 0 && i == row_last - 1) {
+                // Patch the new token's row of the staged tiles (swizzled 16 B chunks).
+                const int chunk = (lane >> 2) ^ (new_slot & 7);
+                const int offset = new_slot * kRowBytes + chunk * 16 + (lane & 3) * 4;
+                *reinterpret_cast<uint32_t *>(stage_tiles + offset) = new_k;
+                *reinterpret_cast<uint32_t *>(stage_tiles + kTileBytes + offset) = new_v;
+            }
+            __syncwarp();
 
             // S^T = K . Q^T over 64 dims (4 k-steps).
             float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -248,13 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
                 pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), a0, a1, a2, a3);
                 pkv::mma_f16_16816(o[mt], a0, a1, a2, a3, b0, b1);
             }
-            // Every lane's shared-memory reads (and the zeroing writes) of this
-            // stage are ordered before the TMA that refills it.
+            // Every lane's shared-memory reads (and the zeroing/patching writes)
+            // of this stage are ordered before the TMA that refills it.
             pkv::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0 && next_fetch < end) {
-                issue_block(&pool_map, flat[next_fetch], num_blocks, k_rows, v_rows, warp,
-                            ktile, bar0 + 8 * stage, error_flag);
+                issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp, ktile,
+                            bar0 + 8 * stage, a.error_flag);
                 ++next_fetch;
             }
         }
@@ -263,10 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
         l0 = warp_sum8(l0);
         l1 = warp_sum8(l1);
         const int head0 = warp * kGroup + 2 * t;  // heads of o[.][0|2] and o[.][1|3]
-        const int cta_first = row_first / blocks_per_cta;
-        const int cta_last = (row_last - 1) / blocks_per_cta;
+        const int cta_first = row_first / a.blocks_per_cta;
+        const int cta_last = (row_last - 1) / a.blocks_per_cta;
         if (cta_first == cta_last) {
-            __half *dst = out + row * out_stride;
+            __half *dst = a.out + row * a.out_stride;
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
                 const int d = 16 * mt + g;
@@ -275,29 +389,65 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
                 dst[head0 * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][2], l0));
                 dst[(head0 + 1) * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][3], l1));
             }
-        } else {
-            const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
-            float *po = part_o + index * kQueryHeads * kHeadDim;
+            continue;
+        }
+        const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
+        float *po = a.part_o + index * kQueryHeads * kHeadDim;
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int d = 16 * mt + g;
-                po[head0 * kHeadDim + d] = o[mt][0];
-                po[(head0 + 1) * kHeadDim + d] = o[mt][1];
-                po[head0 * kHeadDim + d + 8] = o[mt][2];
-                po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
+        for (int mt = 0; mt < 4; ++mt) {
+            const int d = 16 * mt + g;
+            po[head0 * kHeadDim + d] = o[mt][0];
+            po[(head0 + 1) * kHeadDim + d] = o[mt][1];
+            po[head0 * kHeadDim + d + 8] = o[mt][2];
+            po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
+        }
+        if (g == 0) {
+            float *pml = a.part_ml + index * kQueryHeads * 2;
+            pml[head0 * 2 + 0] = m0;
+            pml[head0 * 2 + 1] = l0;
+            pml[(head0 + 1) * 2 + 0] = m1;
+            pml[(head0 + 1) * 2 + 1] = l1;
+        }
+        if constexpr (FUSED) {
+            // Publish this partial; the last of the row's segments for this KV
+            // head merges them (no waiting on other CTAs).
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                const int segments = cta_last - cta_first + 1;
+                last = atomicAdd(&a.counters[row * kKvHeads + warp], 1) == segments - 1;
             }
-            if (g == 0) {
-                float *pml = part_ml + index * kQueryHeads * 2;
-                pml[head0 * 2 + 0] = m0;
-                pml[head0 * 2 + 1] = l0;
-                pml[(head0 + 1) * 2 + 0] = m1;
-                pml[(head0 + 1) * 2 + 1] = l1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                for (int hh = 0; hh < kGroup; ++hh) {
+                    const int head = warp * kGroup + hh;
+                    float m = -INFINITY;
+                    for (int c = cta_first; c <= cta_last; ++c) {
+                        m = fmaxf(m, __ldcg(a.part_ml + ((static_cast<int64_t>(row) + c) * kQueryHeads + head) * 2));
+                    }
+                    float l = 0.f, acc0 = 0.f, acc1 = 0.f;
+                    for (int c = cta_first; c <= cta_last; ++c) {
+                        const int64_t idx = static_cast<int64_t>(row) + c;
+                        const float *ml = a.part_ml + (idx * kQueryHeads + head) * 2;
+                        const float w = pkv::exp2_approx(__ldcg(ml) - m);
+                        l += __ldcg(ml + 1) * w;
+                        const float2 v = __ldcg(reinterpret_cast<const float2 *>(
+                            a.part_o + (idx * kQueryHeads + head) * kHeadDim + 2 * lane));
+                        acc0 += v.x * w;
+                        acc1 += v.y * w;
+                    }
+                    *reinterpret_cast<__half2 *>(a.out + row * a.out_stride + head * kHeadDim + 2 * lane) =
+                        __floats2half2_rn(__fdiv_rn(acc0, l), __fdiv_rn(acc1, l));
+                }
+                if (lane == 0) a.counters[row * kKvHeads + warp] = 0;
             }
         }
     }
 
     if (failed) {
-        if (lane == 0) atomicOr(error_flag, PKV_DEVICE_WAIT_TIMEOUT);
+        if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_WAIT_TIMEOUT);
         // Let the copies this warp issued finish before its shared memory is released.
         for (int c = consumed; c < next_fetch - begin; ++c) {
             pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
@@ -305,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_attention_kernel(
     }
 }
 
-// One warp per (row, query head) of a split row: merge its partials.
+// Second pass of the two-pass variant: one warp per (row, query head) of a
+// split row merges its partials.
 __global__ void __launch_bounds__(256) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
     const int32_t *__restrict__ prefix, int32_t batch, int32_t blocks_per_cta,
@@ -338,7 +489,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Host side: tensor-map cache, launch plan, entry point.
+// Host side: tensor-map cache, launch plan, entry points.
 // ---------------------------------------------------------------------------
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -413,13 +564,24 @@ int configured_stages() {
     return stages;
 }
 
-template <int STAGES>
+template <int STAGES, bool FUSED>
 int prepare_kernel(int *ctas_per_sm) {
-    auto kernel = decode_attention_kernel<STAGES>;
+    auto kernel = decode_kernel<STAGES, FUSED>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<STAGES>());
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, kThreads, smem_bytes<STAGES>());
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("occupancy query: ") + cudaGetErrorString(e));
+    return PKV_OK;
+}
+
+template <int STAGES>
+int prepare_both(int *ctas_per_sm) {
+    int fused = 0;
+    int rc = prepare_kernel<STAGES, false>(ctas_per_sm);
+    if (rc) return rc;
+    rc = prepare_kernel<STAGES, true>(&fused);
+    if (rc) return rc;
+    if (fused < *ctas_per_sm) *ctas_per_sm = fused;
     return PKV_OK;
 }
 
@@ -432,7 +594,7 @@ int device_info(int device, DeviceInfo *info) {
     static std::mutex mutex;
     static std::unordered_map<int, DeviceInfo> cache;
     std::lock_guard<std::mutex> lock(mutex);
-    auto it = cache.find(device * 16 + configured_stages());
+    auto it = cache.find(device);
     if (it != cache.end()) {
         *info = it->second;
         return PKV_OK;
@@ -445,45 +607,42 @@ int device_info(int device, DeviceInfo *info) {
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
     int rc = PKV_OK;
     switch (configured_stages()) {
-        case 4: rc = prepare_kernel<4>(&d.ctas_per_sm); break;
-        case 8: rc = prepare_kernel<8>(&d.ctas_per_sm); break;
-        default: rc = prepare_kernel<6>(&d.ctas_per_sm); break;
+        case 4: rc = prepare_both<4>(&d.ctas_per_sm); break;
+        case 8: rc = prepare_both<8>(&d.ctas_per_sm); break;
+        default: rc = prepare_both<6>(&d.ctas_per_sm); break;
     }
     cudaSetDevice(previous);
     if (rc) return rc;
     if (d.ctas_per_sm < 1) d.ctas_per_sm = 1;
-    cache.emplace(device * 16 + configured_stages(), d);
+    cache.emplace(device, d);
     *info = d;
     return PKV_OK;
 }
 
-}  // namespace
-
-extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
-                               int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes) {
-    pkv::clear_error();
-    if (batch < 1 || total_blocks < batch) {
-        return pkv::fail(PKV_VALUE_ERROR, "decode plan needs batch >= 1 and a nonempty block per row");
+template <bool FUSED>
+void launch_decode(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream) {
+    switch (configured_stages()) {
+        case 4:
+            decode_kernel<4, FUSED><<<grid, kThreads, smem_bytes<4>(), stream>>>(map, args);
+            break;
+        case 8:
+            decode_kernel<8, FUSED><<<grid, kThreads, smem_bytes<8>(), stream>>>(map, args);
+            break;
+        default:
+            decode_kernel<6, FUSED><<<grid, kThreads, smem_bytes<6>(), stream>>>(map, args);
+            break;
     }
-    DeviceInfo info;
-    int rc = device_info(device, &info);
-    if (rc) return rc;
-    const int64_t slots = static_cast<int64_t>(info.sms) * info.ctas_per_sm;
-    const int32_t per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
-    const int32_t grid = (total_blocks + per_cta - 1) / per_cta;
-    *out_grid = grid;
-    *out_blocks_per_cta = per_cta;
-    *out_workspace_bytes = (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
-    return PKV_OK;
 }
 
-extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer,
-                                    const void *query, int64_t query_stride, const int32_t *lengths,
-                                    const int32_t *prefix, const int32_t *flat, int32_t batch,
-                                    int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
-                                    void *out, int64_t out_stride, void *workspace,
-                                    int64_t workspace_bytes, int32_t *error_flag, void *stream) {
-    pkv::clear_error();
+int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
+    return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
+}
+
+// Checks shared by both entry points; fills the common part of LayerArgs.
+int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
+                  const int32_t *lengths, const int32_t *prefix, const int32_t *flat, int32_t batch,
+                  int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
+                  void *workspace, int64_t workspace_bytes, int32_t *error_flag, LayerArgs *args) {
     if (pool == nullptr || query == nullptr || lengths == nullptr || prefix == nullptr ||
         flat == nullptr || out == nullptr || error_flag == nullptr) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: null pointer argument");
@@ -504,53 +663,120 @@ extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_
         (reinterpret_cast<uintptr_t>(workspace) & 15)) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: misaligned tensor");
     }
-    const int64_t needed = (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
-    const bool any_split = grid > 1 && total_blocks > blocks_per_cta;
-    if (any_split && (workspace == nullptr || workspace_bytes < needed)) {
+    if (grid > 1 && (workspace == nullptr || workspace_bytes < workspace_bytes_for(batch, grid))) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: workspace is smaller than the plan needs");
     }
-    int device = 0;
-    cudaGetDevice(&device);
+    LayerArgs &x = *args;
+    x = LayerArgs{};
+    x.query = static_cast<const __half *>(query);
+    x.query_stride = query_stride;
+    x.pool = static_cast<__half *>(const_cast<void *>(pool));
+    x.lengths = lengths;
+    x.prefix = prefix;
+    x.flat = flat;
+    x.batch = batch;
+    x.total_blocks = total_blocks;
+    x.blocks_per_cta = blocks_per_cta;
+    x.num_blocks = num_blocks;
+    x.layer = layer;
+    x.out = static_cast<__half *>(out);
+    x.out_stride = out_stride;
+    x.part_o = static_cast<float *>(workspace);
+    x.part_ml = x.part_o ? x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
+    x.error_flag = error_flag;
+    return PKV_OK;
+}
+
+}  // namespace
+
+extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
+                               int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes) {
+    pkv::clear_error();
+    if (batch < 1 || total_blocks < batch) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode plan needs batch >= 1 and a nonempty block per row");
+    }
     DeviceInfo info;
     int rc = device_info(device, &info);
     if (rc) return rc;
+    const int64_t slots = static_cast<int64_t>(info.sms) * info.ctas_per_sm;
+    const int32_t per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
+    const int32_t grid = (total_blocks + per_cta - 1) / per_cta;
+    *out_grid = grid;
+    *out_blocks_per_cta = per_cta;
+    *out_workspace_bytes = workspace_bytes_for(batch, grid);
+    return PKV_OK;
+}
+
+extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer,
+                                    const void *query, int64_t query_stride, const int32_t *lengths,
+                                    const int32_t *prefix, const int32_t *flat, int32_t batch,
+                                    int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                    void *out, int64_t out_stride, void *workspace,
+                                    int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    LayerArgs args;
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, batch, total_blocks,
+                           grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes, error_flag, &args);
+    if (rc) return rc;
+    int device = 0;
+    cudaGetDevice(&device);
+    DeviceInfo info;
+    if ((rc = device_info(device, &info))) return rc;
     CUtensorMap map;
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
-    float *part_o = static_cast<float *>(workspace);
-    float *part_ml = part_o ? part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const __half *q = static_cast<const __half *>(query);
-    __half *o = static_cast<__half *>(out);
-    switch (configured_stages()) {
-        case 4:
-            decode_attention_kernel<4><<<grid, kThreads, smem_bytes<4>(), s>>>(
-                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
-                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
-            break;
-        case 8:
-            decode_attention_kernel<8><<<grid, kThreads, smem_bytes<8>(), s>>>(
-                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
-                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
-            break;
-        default:
-            decode_attention_kernel<6><<<grid, kThreads, smem_bytes<6>(), s>>>(
-                map, q, query_stride, lengths, prefix, flat, batch, total_blocks, blocks_per_cta,
-                num_blocks, layer, o, out_stride, part_o, part_ml, error_flag);
-            break;
-    }
+    launch_decode<false>(grid, map, args, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         return pkv::fail(PKV_CUDA_ERROR, std::string("decode attention launch failed: ") + cudaGetErrorString(e));
     }
-    if (any_split) {
+    if (grid > 1) {
         const int warps_per_cta = 8;
         const int pairs = batch * kQueryHeads;
         decode_combine_kernel<<<(pairs + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(
-            part_o, part_ml, prefix, batch, blocks_per_cta, o, out_stride);
+            args.part_o, args.part_ml, prefix, batch, blocks_per_cta, args.out, out_stride);
         e = cudaGetLastError();
         if (e != cudaSuccess) {
             return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
         }
+    }
+    return PKV_OK;
+}
+
+extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                int64_t query_stride, const void *key, const void *value, int64_t kv_stride,
+                                const void *rope_table, const int32_t *lengths, const int32_t *prefix,
+                                const int32_t *flat, int32_t batch, int32_t total_blocks, int32_t grid,
+                                int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
+                                int64_t workspace_bytes, int32_t *counters, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    LayerArgs args;
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, batch, total_blocks,
+                           grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes, error_flag, &args);
+    if (rc) return rc;
+    if (key == nullptr || value == nullptr || rope_table == nullptr || (grid > 1 && counters == nullptr)) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode layer: key, value, RoPE table and counters are required");
+    }
+    if ((reinterpret_cast<uintptr_t>(key) & 3) || (reinterpret_cast<uintptr_t>(value) & 3) || kv_stride % 2 ||
+        (reinterpret_cast<uintptr_t>(rope_table) & 3)) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode layer: misaligned tensor");
+    }
+    args.key_new = static_cast<const __half *>(key);
+    args.value_new = static_cast<const __half *>(value);
+    args.new_stride = kv_stride;
+    args.rope_cos = static_cast<const __half *>(rope_table);
+    args.rope_sin = args.rope_cos + PKV_CONTEXT_LIMIT * kRopeHalf;
+    args.counters = counters;
+    int device = 0;
+    cudaGetDevice(&device);
+    DeviceInfo info;
+    if ((rc = device_info(device, &info))) return rc;
+    CUtensorMap map;
+    if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
+    launch_decode<true>(grid, map, args, static_cast<cudaStream_t>(stream));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        return pkv::fail(PKV_CUDA_ERROR, std::string("decode layer launch failed: ") + cudaGetErrorString(e));
     }
     return PKV_OK;
 }

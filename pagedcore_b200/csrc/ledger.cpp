@@ -168,7 +168,8 @@ int key_error(int64_t request) {
 }
 
 // The (blocks, length) a request exposes to readers at `layer`
-// (kv_cache.py:256-263); layer < 0 means the committed view.
+// (kv_cache.py:256-263); layer -1 means the committed view and
+// PKV_VIEW_STAGED the staged view whatever layers were written.
 int resolve_view(pkv_ledger *L, int64_t request, int32_t layer, const Sequence **seq,
                  int32_t *new_block, int32_t *length) {
     auto it = L->sequences.find(request);
@@ -176,10 +177,10 @@ int resolve_view(pkv_ledger *L, int64_t request, int32_t layer, const Sequence *
     *seq = &it->second;
     *new_block = -1;
     *length = it->second.length;
-    if (layer >= 0 && L->staging) {
+    if ((layer >= 0 || layer == PKV_VIEW_STAGED) && L->staging) {
         auto row = L->staged_row.find(request);
         if (row != L->staged_row.end()) {
-            if (layer >= L->staged_written[row->second]) {
+            if (layer != PKV_VIEW_STAGED && layer >= L->staged_written[row->second]) {
                 return fail(PKV_RUNTIME_ERROR, "cannot read an unwritten decode layer");
             }
             *new_block = L->staged_new_block[row->second];
@@ -536,7 +537,7 @@ int pkv_ledger_batch(pkv_ledger *L, const int64_t *requests, int32_t count, int3
     pkv::clear_error();
     int rc = audit(L, requests, count);
     if (rc) return rc;
-    if (layer < 0 || layer >= kLayers) {
+    if ((layer < 0 || layer >= kLayers) && layer != PKV_VIEW_STAGED) {
         return fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
     }
     int32_t total = 0;

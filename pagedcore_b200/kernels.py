@@ -173,3 +173,67 @@ def decode_attention(
         )
     )
     return out
+
+
+def decode_layer(
+    pool: Tensor,
+    layer: int,
+    query: Tensor,
+    key: Tensor,
+    value: Tensor,
+    rope_table: Tensor,
+    lengths: Tensor,
+    prefix: Tensor,
+    flat: Tensor,
+    total_blocks: int,
+    plan: DecodePlan,
+    out: Tensor,
+    workspace: Tensor | None,
+    counters: Tensor,
+    error_flag: Tensor,
+) -> Tensor:
+    """Fused decode layer of a staged batch: RoPE(Q, K), new-token KV write, attention.
+
+    query [B, 32, 64] unrotated, key/value [B, 4, 64] for the new tokens at
+    positions lengths-1 (the staged view); writes attention to ``out``.
+    """
+    batch = query.shape[0]
+    if query.shape[1:] != (_QUERY_HEADS, _HEAD_DIM) or query.stride()[1:] != (_HEAD_DIM, 1):
+        raise ValueError("query must be FP16 [batch, 32, 64] with contiguous rows")
+    if key.shape != (batch, _KV_HEADS, _HEAD_DIM) or value.shape != key.shape:
+        raise ValueError("K and V must share FP16 [batch, 4, 64] on the pool device")
+    if key.stride()[1:] != (_HEAD_DIM, 1) or value.stride() != key.stride():
+        key, value = key.contiguous(), value.contiguous()
+    for name, tensor in (("query", query), ("key", key), ("value", value)):
+        if tensor.dtype != torch.float16:
+            raise ValueError(f"{name} must be FP16")
+    if out.shape != query.shape or out.dtype != torch.float16 or out.stride()[1:] != (_HEAD_DIM, 1):
+        raise ValueError("out must be FP16 [batch, 32, 64] with contiguous rows")
+    check(
+        lib.pkv_decode_layer(
+            _ptr(pool),
+            pool.shape[2],
+            layer,
+            _ptr(query),
+            query.stride(0),
+            _ptr(key),
+            _ptr(value),
+            key.stride(0),
+            _ptr(rope_table),
+            _ptr(lengths),
+            _ptr(prefix),
+            _ptr(flat),
+            batch,
+            total_blocks,
+            plan.grid,
+            plan.blocks_per_cta,
+            _ptr(out),
+            out.stride(0),
+            _ptr(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            _ptr(counters),
+            _ptr(error_flag),
+            _stream(pool.device),
+        )
+    )
+    return out

@@ -29,6 +29,7 @@ import torch
 from torch import Tensor
 
 from pagedcore_b200 import kernels
+from pagedcore_b200._lib import VIEW_STAGED as _VIEW_STAGED
 from pagedcore_b200._lib import device_error_message
 from pagedcore_b200.config import PagedCoreConfig
 from pagedcore_b200.engine_types import BlockId, BlockTable, CapacityCounts, KVReservation, RequestId
@@ -91,8 +92,9 @@ class _Staged:
     slots: Tensor  # int32 device [B]
     positions: Tensor  # int32 device [B]
     host_positions: np.ndarray
-    written: int = 0  # layers written for every row by write_decode_batch
+    written: int = 0  # layers written for every row by write_decode_batch / decode_layer
     batch: DecodeBatch | None = None
+    staged_batch: DecodeBatch | None = None  # staged view of every row, for decode_layer
 
 
 class KVAllocator:
@@ -126,6 +128,7 @@ class KVAllocator:
         self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
         self._rope = device_table(pool.device)
         self._workspace: Tensor | None = None
+        self._counters: Tensor | None = None
 
     # -- plumbing -------------------------------------------------------------
     @property
@@ -169,11 +172,19 @@ class KVAllocator:
             self._workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
         return self._workspace
 
+    def _counters_for(self, batch: int) -> Tensor:
+        """Split-merge counters of the fused decode layer ([B][4] int32, kept at zero)."""
+        if self._counters is None or self._counters.numel() < batch * 4:
+            self._counters = torch.zeros(batch * 4, dtype=torch.int32, device=self._pool.device)
+        return self._counters
+
     def check_device_errors(self) -> None:
         """Synchronise and raise if a kernel flagged an out-of-range block or position."""
         flag = int(self._error.item())
         if flag:
             self._error.zero_()
+            if self._counters is not None:
+                self._counters.zero_()
             raise RuntimeError(device_error_message(flag))
 
     # -- reference API ----------------------------------------------------------
@@ -350,6 +361,59 @@ class KVAllocator:
         staged.written = layer + 1
         return None if query_out is None else query_out[0]
 
+    @torch.inference_mode()
+    def decode_layer(
+        self, layer_index: int, query: Tensor, key: Tensor, value: Tensor, *, out: Tensor | None = None
+    ) -> Tensor:
+        """One decode layer of the staged batch in one launch.
+
+        Fuses, for every staged row in staging order, ``write_decode_layer``
+        of the new token (K given unrotated, rotated at the row's position),
+        the RoPE of ``query`` and block-table attention over the row's
+        context including the new token.  query FP16 [B, 32, 64] (unrotated),
+        key/value FP16 [B, 4, 64]; returns the FP16 [B, 32, 64] attention.
+        """
+        self._check_worker()
+        staged = self._staged
+        if staged is None:
+            raise RuntimeError("decode writes require a staged append")
+        layer = layer_index if type(layer_index) is int else -1
+        self._ledger.decode_check(-1, layer)
+        count = len(staged.requests)
+        if query.shape != (count, 32, 64) or query.dtype != torch.float16 or query.device != self._pool.device:
+            raise ValueError("query must be FP16 [batch, 32, 64] on the pool device")
+        if (
+            key.shape != (count, 4, 64)
+            or value.shape != key.shape
+            or key.dtype != torch.float16
+            or value.dtype != torch.float16
+            or key.device != self._pool.device
+            or value.device != self._pool.device
+        ):
+            raise ValueError("K and V must share FP16 [batch, 4, 64] on the pool device")
+        batch = self.staged_decode_batch()
+        if out is None:
+            out = torch.empty((count, 32, 64), dtype=torch.float16, device=self._pool.device)
+        if query.stride()[1:] != (64, 1):
+            query = query.contiguous()
+        kernels.decode_layer(
+            self._pool, layer, query, key, value, self._rope, batch.lengths, batch.prefix, batch.flat,
+            batch.total_blocks, batch.plan, out, self._workspace_for(batch.plan.workspace_bytes),
+            self._counters_for(count), self._error,
+        )
+        self._ledger.decode_mark(-1, layer)
+        staged.written = layer + 1
+        return out
+
+    def staged_decode_batch(self) -> DecodeBatch:
+        """Device tables of the staged batch with every row's new token included."""
+        staged = self._staged
+        if staged is None:
+            raise RuntimeError("decode writes require a staged append")
+        if staged.staged_batch is None:
+            staged.staged_batch = self._upload_batch(staged.requests, staged.handles, _VIEW_STAGED)
+        return staged.staged_batch
+
     def decode_positions(self) -> np.ndarray:
         """RoPE positions (cached lengths before the append) of the staged rows."""
         if self._staged is None:
@@ -413,19 +477,25 @@ class KVAllocator:
         handles = np.fromiter(
             (self._handle(r, i + 1) for i, r in enumerate(request_ids)), dtype=np.int64, count=len(request_ids)
         )
+        batch = self._upload_batch(request_ids, handles, layer_index)
+        if staged is not None and request_ids == staged.requests and layer_index < staged.written:
+            staged.batch = batch
+        return batch
+
+    def _upload_batch(self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int) -> DecodeBatch:
         count = len(request_ids)
         if count == 0:
             raise ValueError("attention requires a nonempty batch")
         host = np.empty(2 * count + 1 + 129 * count, dtype=np.int32)
         try:
-            total = self._ledger.batch_into(handles, layer_index, host)
+            total = self._ledger.batch_into(handles, layer, host)
         except KeyError as error:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
         used = 2 * count + 1 + total
         device = self._upload_i32(host[:used])
         plan = kernels.decode_plan(self._pool.device, count, total)
-        batch = DecodeBatch(
+        return DecodeBatch(
             requests=request_ids,
             lengths=device[:count],
             prefix=device[count : 2 * count + 1],
@@ -434,9 +504,6 @@ class KVAllocator:
             plan=plan,
             host_lengths=host[:count].copy(),
         )
-        if staged is not None and request_ids == staged.requests and layer_index < staged.written:
-            staged.batch = batch
-        return batch
 
     def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
         """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""
