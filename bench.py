@@ -318,11 +318,15 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     # new token's K/V in (1 KiB) and written to the pool (1 KiB), lengths and
     # prefix, and the split partials written then read back (32 heads x 66 FP32
     # per segment of a split row).
+    plan_info = {}
+
     def layer_bytes() -> float:
         with allocator.append_decode(requests):
             batch = allocator.staged_decode_batch()
             for layer in range(LAYERS):
                 allocator.decode_layer(layer, *(x[layer] for x in device_inputs[0]), out=out[layer])
+        plan_info.update(grid=batch.plan.grid, blocks_per_cta=batch.plan.blocks_per_cta,
+                         total_blocks=batch.total_blocks)
         lengths = batch.host_lengths.astype(np.int64)
         plan = batch.plan
         blocks = (lengths + 15) // 16
@@ -414,6 +418,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "algorithmic_bytes_per_launch": layer_bytes_per_launch,
+                "plan": plan_info,
                 "avg_launch_ms": launch_ms,
                 "traffic": traffic,
             },

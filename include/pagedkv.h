@@ -189,34 +189,35 @@ int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t
  * over the lengths[b] cached tokens of row b at pool layer `layer`, FP32
  * accumulation, one FP16 rounding.  query: FP16 [batch][32][64] with row
  * stride query_stride (elements); out likewise with out_stride.
- * lengths[batch], prefix[batch+1], flat[total_blocks]: int32 device arrays
- * as written by pkv_ledger_batch.  grid / blocks_per_cta / workspace come from
- * pkv_decode_plan for the same (batch, total_blocks).  Two launches: the
- * split kernel and, when some row is split across CTAs, the combine kernel. */
+ * lengths[batch], prefix[batch+1] (prefix[0] == 0), flat[total_blocks]:
+ * int32 device arrays as written by pkv_ledger_batch.  grid / blocks_per_cta
+ * / workspace come from pkv_decode_plan for the same (batch, total_blocks).
+ * cta_rows (nullable): int32 [grid][2], for CTA g the row containing global
+ * block g*blocks_per_cta and that row's first block prefix[row]; without it
+ * every CTA searches prefix.  Two launches: the split kernel and, when
+ * grid > 1, the combine kernel as its programmatic dependent. */
 int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                          int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
-                         const int32_t *flat, int32_t batch, int32_t total_blocks, int32_t grid,
-                         int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
+                         const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
+                         int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
                          int64_t workspace_bytes, int32_t *error_flag, void *stream);
 
-/* One decode layer for a staged batch in one launch: the fused form of
- * write_decode_layer (kv_cache.py:221-246) + apply_rope on Q and K
- * (dense.py:33-61) + paged_attention (attention.py:14-53).  For every row b:
- * the new token sits at position lengths[b]-1 (lengths/prefix/flat from
- * pkv_ledger_batch with PKV_VIEW_STAGED); its K (rotated) and V are written
- * to its pool slot at `layer`, Q is rotated at the same position, and the
- * attention over all lengths[b] tokens is written to out.  query: unrotated
- * FP16 [batch][32][64] (rows query_stride apart); key/value: FP16
- * [batch][4][64] (rows kv_stride apart); rope_table as for pkv_append_kv.
- * Split rows are merged inside the launch: counters is an int32 [batch][4]
- * device array that must be zero before the first call; the kernel leaves it
- * zero again (reset it after a device error).  Same plan and workspace as
- * pkv_decode_attention. */
+/* One decode layer for a staged batch: the fused form of write_decode_layer
+ * (kv_cache.py:221-246) + apply_rope on Q and K (dense.py:33-61) +
+ * paged_attention (attention.py:14-53).  For every row b the new token sits
+ * at position lengths[b]-1 (lengths/prefix/flat from pkv_ledger_batch with
+ * PKV_VIEW_STAGED); its K (rotated) and V are written to its pool slot at
+ * `layer`, Q is rotated at the same position, and the attention over all
+ * lengths[b] tokens is written to out.  query: unrotated FP16 [batch][32][64]
+ * (rows query_stride apart); key/value: FP16 [batch][4][64] (rows kv_stride
+ * apart); rope_table as for pkv_append_kv.  Plan, workspace and cta_rows as
+ * for pkv_decode_attention; one split launch plus, when grid > 1, the
+ * combine launch. */
 int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
                      const void *key, const void *value, int64_t kv_stride, const void *rope_table,
-                     const int32_t *lengths, const int32_t *prefix, const int32_t *flat, int32_t batch,
-                     int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
-                     void *workspace, int64_t workspace_bytes, int32_t *counters, int32_t *error_flag,
+                     const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
+                     int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
+                     int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
                      void *stream);
 
 #ifdef __cplusplus

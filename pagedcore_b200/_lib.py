@@ -102,6 +102,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # lengths
             c_void_p,  # prefix
             c_void_p,  # flat
+            c_void_p,  # cta_rows
             c_int32,  # batch
             c_int32,  # total_blocks
             c_int32,  # grid
@@ -110,7 +111,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int64,  # out_stride
             c_void_p,  # workspace
             c_int64,  # workspace_bytes
-            c_void_p,  # counters
             c_void_p,  # error_flag
             c_void_p,  # stream
         ],
@@ -118,24 +118,25 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_decode_attention": (
         c_int,
         [
-            c_void_p,
-            c_int32,
-            c_int32,
-            c_void_p,
-            c_int64,
-            c_void_p,
-            c_void_p,
-            c_void_p,
-            c_int32,
-            c_int32,
-            c_int32,
-            c_int32,
-            c_void_p,
-            c_int64,
-            c_void_p,
-            c_int64,
-            c_void_p,
-            c_void_p,
+            c_void_p,  # pool
+            c_int32,  # num_blocks
+            c_int32,  # layer
+            c_void_p,  # query
+            c_int64,  # query_stride
+            c_void_p,  # lengths
+            c_void_p,  # prefix
+            c_void_p,  # flat
+            c_void_p,  # cta_rows
+            c_int32,  # batch
+            c_int32,  # total_blocks
+            c_int32,  # grid
+            c_int32,  # blocks_per_cta
+            c_void_p,  # out
+            c_int64,  # out_stride
+            c_void_p,  # workspace
+            c_int64,  # workspace_bytes
+            c_void_p,  # error_flag
+            c_void_p,  # stream
         ],
     ),
 }

@@ -39,7 +39,9 @@
 //   * two-pass (paged_attention's drop-in path): decode_combine_kernel runs
 //     after the split kernel;
 //   * fused decode layer: the last warp to finish a (row, KV head) - counted
-//     with one atomic per warp, no waiting - merges the partials itself.
+//     with one atomic per warp, no waiting - merges the partials itself.  Only
+//     the first and last segments of a CTA's range can be split, so each warp
+//     publishes at most two partials, after its whole range is streamed.
 //
 // The fused decode-layer variant also does the layer's KV append: it applies
 // RoPE to Q (every CTA of the row, in registers) and to the new token's K
@@ -106,7 +108,7 @@ struct LayerArgs {
     int64_t out_stride;
     float *part_o;             // [(B + grid)][32][64]
     float *part_ml;            // [(B + grid)][32][2]
-    int32_t *counters;         // FUSED: [B][4], zero between launches
+    const int32_t *cta_rows;   // [grid][2]: first row of each CTA's range and its first block (or null)
     int32_t *error_flag;
 };
 
@@ -146,12 +148,28 @@ __device__ __forceinline__ uint32_t rope_half2(uint32_t x, uint32_t rot, bool ne
 
 __device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
+// One step of the split-partial merge, in a fixed operation order shared by
+// the fused kernel and the two-pass combine kernel (so both give the same
+// bits): fold partial (m, l, o0, o1) into the running (M, L, A0, A1).
+__device__ __forceinline__ void merge_partial(float &M, float &L, float &A0, float &A1, float m, float l, float o0,
+                                              float o1) {
+    const float mn = fmaxf(M, m);
+    const float a = pkv::exp2_approx(M - mn);
+    const float b = pkv::exp2_approx(m - mn);
+    L = __fmaf_rn(L, a, __fmul_rn(l, b));
+    A0 = __fmaf_rn(A0, a, __fmul_rn(o0, b));
+    A1 = __fmaf_rn(A1, a, __fmul_rn(o1, b));
+    M = mn;
+}
+
 // Fetch one block's K and V boxes of KV head `head` into a pipeline stage
 // (called by one lane).  An out-of-range block id sets the error flag and
 // completes the stage's phase without data, so no waiter is left behind.
 __device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t block, int32_t num_blocks,
                                             int32_t k_rows, int32_t v_rows, int head, uint32_t dst,
-                                            uint32_t bar, int32_t *error_flag) {
+                                            uint32_t bar, int32_t *error_flag, uint32_t after = 0u) {
+    // `after` ties the issue to a value computed from the stage's last reads.
+    asm volatile("" ::"r"(after) : "memory");
     if (block < 0 || block >= num_blocks) {
         atomicOr(error_flag, PKV_DEVICE_BAD_BLOCK);
         pkv::mbar_arrive(bar);
@@ -160,6 +178,73 @@ __device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t bloc
     pkv::mbar_arrive_expect_tx(bar, kStageBytes);
     pkv::tma_load_3d(dst, map, 0, head, k_rows + block * kBlockTokens, bar);
     pkv::tma_load_3d(dst + kTileBytes, map, 0, head, v_rows + block * kBlockTokens, bar);
+}
+
+// Per-row inputs of a segment.  The head (two int32) is loaded two rows
+// ahead, the body one row ahead, so that row switches never wait on
+// global-memory latency behind the KV stream.
+struct RowHead {
+    int32_t last;    // prefix[row + 1]
+    int32_t length;  // lengths[row]
+};
+
+struct RowBody {
+    uint32_t q[4][2];      // raw Q fragments of this warp's 8 heads
+    uint32_t cs[4], sn[4]; // FUSED: cos/sin pairs for Q dims (16*ks + 8*h + 2t) & 31, index 2*ks + h
+    uint32_t kcs, ksn;     // FUSED: cos/sin pair for the new K's dims (2*lane) & 31
+    uint32_t k_own, k_partner, v_own;  // FUSED: new token's K (dims 2*lane, partner) and V
+    int32_t last_block;    // FUSED: flat[last - 1]
+};
+
+__device__ __forceinline__ RowHead row_head(const LayerArgs &a, int row) {
+    RowHead h;
+    h.last = a.prefix[row + 1];
+    h.length = a.lengths[row];
+    return h;
+}
+
+__device__ __forceinline__ int clamp_position(const LayerArgs &a, int length, int lane) {
+    int pos = length - 1;
+    if (pos < 0 || pos >= PKV_CONTEXT_LIMIT) {
+        if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_POSITION);
+        pos = 0;
+    }
+    return pos;
+}
+
+template <bool FUSED>
+__device__ __forceinline__ void row_body(const LayerArgs &a, int row, const RowHead &h, int warp, int lane,
+                                         RowBody &m) {
+    const int g = lane >> 2, t = lane & 3;
+    const __half *q = a.query + row * a.query_stride + (warp * kGroup + g) * kHeadDim;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+        m.q[ks][0] = ld32(q + 16 * ks + 2 * t);
+        m.q[ks][1] = ld32(q + 16 * ks + 8 + 2 * t);
+    }
+    if constexpr (FUSED) {
+        const int pos = clamp_position(a, h.length, lane);
+        const __half *cs = a.rope_cos + pos * kRopeHalf;
+        const __half *sn = a.rope_sin + pos * kRopeHalf;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const int d = 16 * ks + 8 * hh + 2 * t;
+                m.cs[2 * ks + hh] = ld32(cs + d);
+                m.sn[2 * ks + hh] = ld32(sn + d);
+            }
+        }
+        const int d = 2 * lane;
+        const int dk = d & (kRopeHalf - 1);
+        m.kcs = ld32(cs + dk);
+        m.ksn = ld32(sn + dk);
+        const __half *kn = a.key_new + row * a.new_stride + warp * kHeadDim;
+        m.k_own = ld32(kn + d);
+        m.k_partner = ld32(kn + ((d + kRopeHalf) & (kHeadDim - 1)));
+        m.v_own = ld32(a.value_new + row * a.new_stride + warp * kHeadDim + d);
+        m.last_block = a.flat[h.last - 1];
+    }
 }
 
 template <int STAGES, bool FUSED>
@@ -204,69 +289,71 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
-    // First row of the range: the largest b with prefix[b] <= begin.
-    int lo = 0, hi = a.batch - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (a.prefix[mid] <= begin) lo = mid; else hi = mid - 1;
+    // First row of the range (the largest b with prefix[b] <= begin) and its
+    // first block: from the host's per-CTA table, else a 32-way search.
+    int row = 0, row_first = 0;
+    if (a.cta_rows != nullptr) {
+        row = a.cta_rows[2 * blockIdx.x];
+        row_first = a.cta_rows[2 * blockIdx.x + 1];
+    } else {
+        int lo = 0, hi = a.batch - 1, lo_value = 0;
+        while (hi > lo) {
+            const int step = (hi - lo + 32) / 32;
+            const int probe = lo + lane * step;
+            const int value = probe <= hi ? a.prefix[probe] : INT32_MAX;
+            const unsigned mask = __ballot_sync(0xffffffffu, value <= begin);
+            const int best = 31 - __clz(mask);  // lane 0 probes lo, whose prefix is <= begin
+            lo_value = __shfl_sync(0xffffffffu, value, best);
+            lo += best * step;
+            hi = min(hi, lo + step - 1);
+        }
+        row = lo;
+        row_first = lo_value;
     }
+
+    RowHead head = row_head(a, row);
+    RowHead head1 = row + 1 < a.batch ? row_head(a, row + 1) : RowHead{0, 0};
+    RowHead head2 = row + 2 < a.batch ? row_head(a, row + 2) : RowHead{0, 0};
+    RowBody body, body1;
+    row_body<FUSED>(a, row, head, warp, lane, body);
 
     int consumed = 0;
     bool failed = false;
-    for (int row = lo, i = begin; i < end; ++row) {
-        const int row_first = a.prefix[row];
-        const int row_last = a.prefix[row + 1];
+    int i = begin;
+    while (true) {
+        const int row_last = head.last;
         const int seg_end = min(end, row_last);
-        const int length = a.lengths[row];
+        const int length = head.length;
+        const bool has_next = row_last < end;
+        // Prefetch: the next row's body (its head arrived a segment ago) and
+        // the head three rows ahead.
+        if (has_next) row_body<FUSED>(a, row + 1, head1, warp, lane, body1);
+        const RowHead head3 = (has_next && row + 3 < a.batch) ? row_head(a, row + 3) : RowHead{0, 0};
 
-        // Q^T fragments (B operand) of this warp's 8 query heads: lane holds
-        // dims 16ks + 2t + {0,1} and 16ks + 8 + 2t + {0,1} of head 8*warp + g.
-        const __half *q = a.query + row * a.query_stride + (warp * kGroup + g) * kHeadDim;
+        // Q^T fragments (B operand): lane holds dims 16ks + 2t + {0,1} and
+        // 16ks + 8 + 2t + {0,1} of head 8*warp + g.
         uint32_t qf[4][2];
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-            qf[ks][0] = ld32(q + 16 * ks + 2 * t);
-            qf[ks][1] = ld32(q + 16 * ks + 8 + 2 * t);
-        }
-
-        // Fused append: the new token sits at position length-1 of the row.
         uint32_t new_k = 0, new_v = 0;
         int new_slot = -1;
         if constexpr (FUSED) {
-            int pos = length - 1;
-            if (pos < 0 || pos >= PKV_CONTEXT_LIMIT) {
-                if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_POSITION);
-                pos = 0;
-            }
-            // RoPE of Q in registers: dims d < 32 pair with d + 32 (k-step ks + 2).
-            const __half *cs = a.rope_cos + pos * kRopeHalf;
-            const __half *sn = a.rope_sin + pos * kRopeHalf;
-            uint32_t rq[4][2];
+            // RoPE of Q in registers: dims d < 32 pair with d + 32 (k-step ks ^ 2).
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int d = (16 * ks + 8 * h + 2 * t) & (kRopeHalf - 1);
-                    rq[ks][h] = rope_half2(qf[ks][h], qf[ks ^ 2][h], ks < 2, ld32(cs + d), ld32(sn + d));
+                    const int c = 2 * (ks & 1) + h;
+                    qf[ks][h] = rope_half2(body.q[ks][h], body.q[ks ^ 2][h], ks < 2, body.cs[c], body.sn[c]);
                 }
-            }
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                qf[ks][0] = rq[ks][0];
-                qf[ks][1] = rq[ks][1];
             }
             if (seg_end == row_last) {
                 // This CTA holds the row's last block: rotate the new K (lane owns
                 // dims 2*lane, 2*lane+1 of head `warp`) and write K/V to the pool.
-                const __half *kn = a.key_new + row * a.new_stride + warp * kHeadDim;
-                const __half *vn = a.value_new + row * a.new_stride + warp * kHeadDim;
                 const int d = 2 * lane;
-                new_k = rope_half2(ld32(kn + d), ld32(kn + ((d + kRopeHalf) & (kHeadDim - 1))), d < kRopeHalf,
-                                   ld32(cs + (d & (kRopeHalf - 1))), ld32(sn + (d & (kRopeHalf - 1))));
-                new_v = ld32(vn + d);
-                new_slot = pos & (kBlockTokens - 1);
-                const int32_t block = a.flat[row_last - 1];
-                if (block >= 0 && block < a.num_blocks) {
+                new_k = rope_half2(body.k_own, body.k_partner, d < kRopeHalf, body.kcs, body.ksn);
+                new_v = body.v_own;
+                new_slot = (length - 1) & (kBlockTokens - 1);
+                const int32_t block = body.last_block;
+                if (block >= 0 && block < a.num_blocks && length >= 1 && length <= PKV_CONTEXT_LIMIT) {
                     const int64_t base =
                         (((static_cast<int64_t>(a.layer) * 2) * a.num_blocks + block) * kBlockTokens + new_slot) *
                             (kKvHeads * kHeadDim) +
@@ -274,7 +361,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int64_t v_offset = static_cast<int64_t>(a.num_blocks) * kBlockTokens * kKvHeads * kHeadDim;
                     *reinterpret_cast<uint32_t *>(a.pool + base) = new_k;
                     *reinterpret_cast<uint32_t *>(a.pool + base + v_offset) = new_v;
+                } else {
+                    new_slot = -1;
+                    if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
                 }
+            }
+        } else {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                qf[ks][0] = body.q[ks][0];
+                qf[ks][1] = body.q[ks][1];
             }
         }
 
@@ -294,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t vtile = ktile + kTileBytes;
             const int valid = min(kBlockTokens, length - (i - row_first) * kBlockTokens);
             uint8_t *stage_tiles = warp_tiles + stage * kStageBytes;
+            bool wrote = false;
             if (valid < kBlockTokens) {
                 // Zero the V rows of unwritten slots: P is 0 there, but 0 * NaN is NaN.
                 uint8_t *vrows = stage_tiles + kTileBytes;
@@ -301,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4 *>(vrows + (valid + idx / 8) * kRowBytes + (idx % 8) * 16) =
                         make_uint4(0, 0, 0, 0);
                 }
+                wrote = true;
             }
             if (FUSED && new_slot >= 0 && i == row_last - 1) {
                 // Patch the new token's row of the staged tiles (swizzled 16 B chunks).
@@ -308,19 +406,52 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int offset = new_slot * kRowBytes + chunk * 16 + (lane & 3) * 4;
                 *reinterpret_cast<uint32_t *>(stage_tiles + offset) = new_k;
                 *reinterpret_cast<uint32_t *>(stage_tiles + kTileBytes + offset) = new_v;
+                wrote = true;
             }
-            __syncwarp();
+            if (wrote) __syncwarp();
 
-            // S^T = K . Q^T over 64 dims (4 k-steps).
-            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            // K (row-major tokens x dims) and V^T fragments of the whole block.
+            uint32_t kf[4][4], vf[4][4];
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
                 const int mat = lane >> 3;
                 const int tok = (lane & 7) + ((mat & 1) << 3);
                 const int chunk = 2 * ks + (mat >> 1);
-                uint32_t a0, a1, a2, a3;
-                pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), a0, a1, a2, a3);
-                pkv::mma_f16_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), kf[ks][0], kf[ks][1],
+                                 kf[ks][2], kf[ks][3]);
+            }
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int mat = lane >> 3;
+                const int tok = (lane & 7) + ((mat >> 1) << 3);
+                const int chunk = 2 * mt + (mat & 1);
+                pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), vf[mt][0], vf[mt][1],
+                                       vf[mt][2], vf[mt][3]);
+            }
+            // Hand the stage back to the TMA pipeline before the math.  The
+            // refill is issued after every lane holds its fragments (it takes a
+            // value computed from all of them, after a warp barrier) and after a
+            // proxy fence ordering this stage's generic accesses before it.
+            {
+                uint32_t ready = 0;
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                    ready ^= kf[x][0] ^ kf[x][1] ^ kf[x][2] ^ kf[x][3] ^ vf[x][0] ^ vf[x][1] ^ vf[x][2] ^ vf[x][3];
+                }
+                asm volatile("" ::"r"(ready) : "memory");
+                pkv::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && next_fetch < end) {
+                    issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp, ktile,
+                                bar0 + 8 * stage, a.error_flag, ready);
+                    ++next_fetch;
+                }
+            }
+            // S^T = K . Q^T over 64 dims (4 k-steps).
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                pkv::mma_f16_16816(s, kf[ks][0], kf[ks][1], kf[ks][2], kf[ks][3], qf[ks][0], qf[ks][1]);
             }
             // s[0]: (token g, head 2t), s[1]: (g, 2t+1), s[2]: (g+8, 2t), s[3]: (g+8, 2t+1)
             const float s0 = g < valid ? s[0] * kScaleLog2 : -INFINITY;
@@ -355,21 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // O^T += V^T . P^T over 16 tokens (4 dim tiles of 16).
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
-                const int mat = lane >> 3;
-                const int tok = (lane & 7) + ((mat >> 1) << 3);
-                const int chunk = 2 * mt + (mat & 1);
-                uint32_t a0, a1, a2, a3;
-                pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), a0, a1, a2, a3);
-                pkv::mma_f16_16816(o[mt], a0, a1, a2, a3, b0, b1);
-            }
-            // Every lane's shared-memory reads (and the zeroing/patching writes)
-            // of this stage are ordered before the TMA that refills it.
-            pkv::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && next_fetch < end) {
-                issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp, ktile,
-                            bar0 + 8 * stage, a.error_flag);
-                ++next_fetch;
+                pkv::mma_f16_16816(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], b0, b1);
             }
         }
         if (failed) break;
@@ -389,61 +506,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dst[head0 * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][2], l0));
                 dst[(head0 + 1) * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][3], l1));
             }
-            continue;
-        }
-        const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
-        float *po = a.part_o + index * kQueryHeads * kHeadDim;
+        } else {
+            const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
+            float *po = a.part_o + index * kQueryHeads * kHeadDim;
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-            const int d = 16 * mt + g;
-            po[head0 * kHeadDim + d] = o[mt][0];
-            po[(head0 + 1) * kHeadDim + d] = o[mt][1];
-            po[head0 * kHeadDim + d + 8] = o[mt][2];
-            po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
-        }
-        if (g == 0) {
-            float *pml = a.part_ml + index * kQueryHeads * 2;
-            pml[head0 * 2 + 0] = m0;
-            pml[head0 * 2 + 1] = l0;
-            pml[(head0 + 1) * 2 + 0] = m1;
-            pml[(head0 + 1) * 2 + 1] = l1;
-        }
-        if constexpr (FUSED) {
-            // Publish this partial; the last of the row's segments for this KV
-            // head merges them (no waiting on other CTAs).
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) {
-                const int segments = cta_last - cta_first + 1;
-                last = atomicAdd(&a.counters[row * kKvHeads + warp], 1) == segments - 1;
+            for (int mt = 0; mt < 4; ++mt) {
+                const int d = 16 * mt + g;
+                po[head0 * kHeadDim + d] = o[mt][0];
+                po[(head0 + 1) * kHeadDim + d] = o[mt][1];
+                po[head0 * kHeadDim + d + 8] = o[mt][2];
+                po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
             }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence();
-                for (int hh = 0; hh < kGroup; ++hh) {
-                    const int head = warp * kGroup + hh;
-                    float m = -INFINITY;
-                    for (int c = cta_first; c <= cta_last; ++c) {
-                        m = fmaxf(m, __ldcg(a.part_ml + ((static_cast<int64_t>(row) + c) * kQueryHeads + head) * 2));
-                    }
-                    float l = 0.f, acc0 = 0.f, acc1 = 0.f;
-                    for (int c = cta_first; c <= cta_last; ++c) {
-                        const int64_t idx = static_cast<int64_t>(row) + c;
-                        const float *ml = a.part_ml + (idx * kQueryHeads + head) * 2;
-                        const float w = pkv::exp2_approx(__ldcg(ml) - m);
-                        l += __ldcg(ml + 1) * w;
-                        const float2 v = __ldcg(reinterpret_cast<const float2 *>(
-                            a.part_o + (idx * kQueryHeads + head) * kHeadDim + 2 * lane));
-                        acc0 += v.x * w;
-                        acc1 += v.y * w;
-                    }
-                    *reinterpret_cast<__half2 *>(a.out + row * a.out_stride + head * kHeadDim + 2 * lane) =
-                        __floats2half2_rn(__fdiv_rn(acc0, l), __fdiv_rn(acc1, l));
-                }
-                if (lane == 0) a.counters[row * kKvHeads + warp] = 0;
+            if (g == 0) {
+                float *pml = a.part_ml + index * kQueryHeads * 2;
+                pml[head0 * 2 + 0] = m0;
+                pml[head0 * 2 + 1] = l0;
+                pml[(head0 + 1) * 2 + 0] = m1;
+                pml[(head0 + 1) * 2 + 1] = l1;
             }
         }
+        if (!has_next) break;
+        ++row;
+        row_first = row_last;
+        head = head1;
+        head1 = head2;
+        head2 = head3;
+        body = body1;
     }
 
     if (failed) {
@@ -453,10 +541,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
         }
     }
+    // The combine kernel (launched as a programmatic dependent) may start.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Second pass of the two-pass variant: one warp per (row, query head) of a
-// split row merges its partials.
+// Second pass: one warp per (row, query head) of a split row merges its
+// partials.  It is launched as a programmatic dependent of the split kernel,
+// so its launch and prologue overlap the split kernel's tail.
 __global__ void __launch_bounds__(256) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
     const int32_t *__restrict__ prefix, int32_t batch, int32_t blocks_per_cta,
@@ -465,27 +556,22 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
     const int lane = threadIdx.x & 31;
     const int row = pair / kQueryHeads;
     const int head = pair % kQueryHeads;
-    if (row >= batch) return;
-    const int cta_first = prefix[row] / blocks_per_cta;
-    const int cta_last = (prefix[row + 1] - 1) / blocks_per_cta;
-    if (cta_first == cta_last) return;  // written directly by the split kernel
-    float m = -INFINITY;
-    for (int c = cta_first; c <= cta_last; ++c) {
-        m = fmaxf(m, part_ml[((static_cast<int64_t>(row) + c) * kQueryHeads + head) * 2]);
+    int cta_first = 0, cta_last = 0;
+    if (row < batch) {
+        cta_first = prefix[row] / blocks_per_cta;
+        cta_last = (prefix[row + 1] - 1) / blocks_per_cta;
     }
-    float l = 0.f, acc0 = 0.f, acc1 = 0.f;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
+    float M = -INFINITY, L = 0.f, A0 = 0.f, A1 = 0.f;
     for (int c = cta_first; c <= cta_last; ++c) {
-        const int64_t index = static_cast<int64_t>(row) + c;
-        const float *ml = part_ml + (index * kQueryHeads + head) * 2;
-        const float w = pkv::exp2_approx(ml[0] - m);
-        l += ml[1] * w;
-        const float2 v = *reinterpret_cast<const float2 *>(
-            part_o + (index * kQueryHeads + head) * kHeadDim + 2 * lane);
-        acc0 += v.x * w;
-        acc1 += v.y * w;
+        const int64_t idx = (static_cast<int64_t>(row) + c) * kQueryHeads + head;
+        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
+        const float2 v = *reinterpret_cast<const float2 *>(part_o + idx * kHeadDim + 2 * lane);
+        merge_partial(M, L, A0, A1, ml.x, ml.y, v.x, v.y);
     }
     *reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + 2 * lane) =
-        __floats2half2_rn(__fdiv_rn(acc0, l), __fdiv_rn(acc1, l));
+        __floats2half2_rn(__fdiv_rn(A0, L), __fdiv_rn(A1, L));
 }
 
 // ---------------------------------------------------------------------------
@@ -554,12 +640,12 @@ int pool_tensor_map(const void *pool, int32_t num_blocks, CUtensorMap *out) {
     return PKV_OK;
 }
 
-// Pipeline depth per warp; PKV_DECODE_STAGES (4, 6 or 8) overrides it.
+// Pipeline depth per warp (4: three CTAs per SM); PKV_DECODE_STAGES (4, 6 or 8) overrides it.
 int configured_stages() {
     static int stages = [] {
         const char *env = std::getenv("PKV_DECODE_STAGES");
-        const int v = env ? std::atoi(env) : 6;
-        return (v == 4 || v == 6 || v == 8) ? v : 6;
+        const int v = env ? std::atoi(env) : 4;
+        return (v == 4 || v == 6 || v == 8) ? v : 4;
     }();
     return stages;
 }
@@ -640,9 +726,9 @@ int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
 
 // Checks shared by both entry points; fills the common part of LayerArgs.
 int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
-                  const int32_t *lengths, const int32_t *prefix, const int32_t *flat, int32_t batch,
-                  int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
-                  void *workspace, int64_t workspace_bytes, int32_t *error_flag, LayerArgs *args) {
+                  const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
+                  int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
+                  int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag, LayerArgs *args) {
     if (pool == nullptr || query == nullptr || lengths == nullptr || prefix == nullptr ||
         flat == nullptr || out == nullptr || error_flag == nullptr) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: null pointer argument");
@@ -674,6 +760,7 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.lengths = lengths;
     x.prefix = prefix;
     x.flat = flat;
+    x.cta_rows = cta_rows;
     x.batch = batch;
     x.total_blocks = total_blocks;
     x.blocks_per_cta = blocks_per_cta;
@@ -684,6 +771,35 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.part_o = static_cast<float *>(workspace);
     x.part_ml = x.part_o ? x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
     x.error_flag = error_flag;
+    return PKV_OK;
+}
+
+// Launch the split kernel, then (when rows can be split) the combine kernel
+// as its programmatic dependent on the same stream.
+template <bool FUSED>
+int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream, const char *what) {
+    launch_decode<FUSED>(grid, map, args, stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string(what) + " launch failed: " + cudaGetErrorString(e));
+    if (grid == 1) return PKV_OK;
+    const int warps_per_cta = 8;
+    const int pairs = args.batch * kQueryHeads;
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3((pairs + warps_per_cta - 1) / warps_per_cta);
+    config.blockDim = dim3(warps_per_cta * 32);
+    config.dynamicSmemBytes = 0;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    e = cudaLaunchKernelEx(&config, decode_combine_kernel, static_cast<const float *>(args.part_o),
+                           static_cast<const float *>(args.part_ml), args.prefix, args.batch, args.blocks_per_cta,
+                           args.out, args.out_stride);
+    if (e != cudaSuccess) {
+        return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
+    }
     return PKV_OK;
 }
 
@@ -709,14 +825,15 @@ extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_bloc
 
 extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer,
                                     const void *query, int64_t query_stride, const int32_t *lengths,
-                                    const int32_t *prefix, const int32_t *flat, int32_t batch,
-                                    int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
-                                    void *out, int64_t out_stride, void *workspace,
-                                    int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+                                    const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
+                                    int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                    void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
+                                    int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
-    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, batch, total_blocks,
-                           grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes, error_flag, &args);
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+                           total_blocks, grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes,
+                           error_flag, &args);
     if (rc) return rc;
     int device = 0;
     cudaGetDevice(&device);
@@ -724,38 +841,23 @@ extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_
     if ((rc = device_info(device, &info))) return rc;
     CUtensorMap map;
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    launch_decode<false>(grid, map, args, s);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        return pkv::fail(PKV_CUDA_ERROR, std::string("decode attention launch failed: ") + cudaGetErrorString(e));
-    }
-    if (grid > 1) {
-        const int warps_per_cta = 8;
-        const int pairs = batch * kQueryHeads;
-        decode_combine_kernel<<<(pairs + warps_per_cta - 1) / warps_per_cta, warps_per_cta * 32, 0, s>>>(
-            args.part_o, args.part_ml, prefix, batch, blocks_per_cta, args.out, out_stride);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) {
-            return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
-        }
-    }
-    return PKV_OK;
+    return launch_pass<false>(grid, map, args, static_cast<cudaStream_t>(stream), "decode attention");
 }
 
 extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                 int64_t query_stride, const void *key, const void *value, int64_t kv_stride,
                                 const void *rope_table, const int32_t *lengths, const int32_t *prefix,
-                                const int32_t *flat, int32_t batch, int32_t total_blocks, int32_t grid,
-                                int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
-                                int64_t workspace_bytes, int32_t *counters, int32_t *error_flag, void *stream) {
+                                const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
+                                int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
+                                void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
-    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, batch, total_blocks,
-                           grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes, error_flag, &args);
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+                           total_blocks, grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes,
+                           error_flag, &args);
     if (rc) return rc;
-    if (key == nullptr || value == nullptr || rope_table == nullptr || (grid > 1 && counters == nullptr)) {
-        return pkv::fail(PKV_VALUE_ERROR, "decode layer: key, value, RoPE table and counters are required");
+    if (key == nullptr || value == nullptr || rope_table == nullptr) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode layer: key, value and RoPE table are required");
     }
     if ((reinterpret_cast<uintptr_t>(key) & 3) || (reinterpret_cast<uintptr_t>(value) & 3) || kv_stride % 2 ||
         (reinterpret_cast<uintptr_t>(rope_table) & 3)) {
@@ -766,17 +868,11 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
     args.new_stride = kv_stride;
     args.rope_cos = static_cast<const __half *>(rope_table);
     args.rope_sin = args.rope_cos + PKV_CONTEXT_LIMIT * kRopeHalf;
-    args.counters = counters;
     int device = 0;
     cudaGetDevice(&device);
     DeviceInfo info;
     if ((rc = device_info(device, &info))) return rc;
     CUtensorMap map;
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
-    launch_decode<true>(grid, map, args, static_cast<cudaStream_t>(stream));
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        return pkv::fail(PKV_CUDA_ERROR, std::string("decode layer launch failed: ") + cudaGetErrorString(e));
-    }
-    return PKV_OK;
+    return launch_pass<true>(grid, map, args, static_cast<cudaStream_t>(stream), "decode layer");
 }

@@ -138,6 +138,7 @@ def decode_attention(
     out: Tensor,
     workspace: Tensor | None,
     error_flag: Tensor,
+    cta_rows: Tensor | None = None,
 ) -> Tensor:
     """Split-K block-table attention of FP16 query [B, 32, 64] into ``out``."""
     device = pool.device
@@ -160,6 +161,7 @@ def decode_attention(
             _ptr(lengths),
             _ptr(prefix),
             _ptr(flat),
+            _ptr(cta_rows),
             batch,
             total_blocks,
             plan.grid,
@@ -189,8 +191,8 @@ def decode_layer(
     plan: DecodePlan,
     out: Tensor,
     workspace: Tensor | None,
-    counters: Tensor,
     error_flag: Tensor,
+    cta_rows: Tensor | None = None,
 ) -> Tensor:
     """Fused decode layer of a staged batch: RoPE(Q, K), new-token KV write, attention.
 
@@ -223,6 +225,7 @@ def decode_layer(
             _ptr(lengths),
             _ptr(prefix),
             _ptr(flat),
+            _ptr(cta_rows),
             batch,
             total_blocks,
             plan.grid,
@@ -231,7 +234,6 @@ def decode_layer(
             out.stride(0),
             _ptr(workspace),
             0 if workspace is None else workspace.numel() * workspace.element_size(),
-            _ptr(counters),
             _ptr(error_flag),
             _stream(pool.device),
         )

@@ -30,7 +30,7 @@ from torch import Tensor
 
 from pagedcore_b200 import kernels
 from pagedcore_b200._lib import VIEW_STAGED as _VIEW_STAGED
-from pagedcore_b200._lib import device_error_message
+from pagedcore_b200._lib import check, device_error_message, lib
 from pagedcore_b200.config import PagedCoreConfig
 from pagedcore_b200.engine_types import BlockId, BlockTable, CapacityCounts, KVReservation, RequestId
 from pagedcore_b200.ledger import BlockLedger
@@ -79,6 +79,7 @@ class DecodeBatch:
     lengths: Tensor
     prefix: Tensor
     flat: Tensor
+    cta_rows: Tensor  # [grid][2]: first row of each CTA's block range and its first block
     total_blocks: int
     plan: kernels.DecodePlan
     host_lengths: np.ndarray
@@ -95,6 +96,7 @@ class _Staged:
     written: int = 0  # layers written for every row by write_decode_batch / decode_layer
     batch: DecodeBatch | None = None
     staged_batch: DecodeBatch | None = None  # staged view of every row, for decode_layer
+    launch_args: tuple | None = None  # fixed pkv_decode_layer arguments of this step
 
 
 class KVAllocator:
@@ -128,7 +130,6 @@ class KVAllocator:
         self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
         self._rope = device_table(pool.device)
         self._workspace: Tensor | None = None
-        self._counters: Tensor | None = None
 
     # -- plumbing -------------------------------------------------------------
     @property
@@ -172,19 +173,11 @@ class KVAllocator:
             self._workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
         return self._workspace
 
-    def _counters_for(self, batch: int) -> Tensor:
-        """Split-merge counters of the fused decode layer ([B][4] int32, kept at zero)."""
-        if self._counters is None or self._counters.numel() < batch * 4:
-            self._counters = torch.zeros(batch * 4, dtype=torch.int32, device=self._pool.device)
-        return self._counters
-
     def check_device_errors(self) -> None:
         """Synchronise and raise if a kernel flagged an out-of-range block or position."""
         flag = int(self._error.item())
         if flag:
             self._error.zero_()
-            if self._counters is not None:
-                self._counters.zero_()
             raise RuntimeError(device_error_message(flag))
 
     # -- reference API ----------------------------------------------------------
@@ -391,19 +384,38 @@ class KVAllocator:
             or value.device != self._pool.device
         ):
             raise ValueError("K and V must share FP16 [batch, 4, 64] on the pool device")
-        batch = self.staged_decode_batch()
-        if out is None:
-            out = torch.empty((count, 32, 64), dtype=torch.float16, device=self._pool.device)
         if query.stride()[1:] != (64, 1):
             query = query.contiguous()
-        kernels.decode_layer(
-            self._pool, layer, query, key, value, self._rope, batch.lengths, batch.prefix, batch.flat,
-            batch.total_blocks, batch.plan, out, self._workspace_for(batch.plan.workspace_bytes),
-            self._counters_for(count), self._error,
+        if key.stride()[1:] != (64, 1) or value.stride() != key.stride():
+            key, value = key.contiguous(), value.contiguous()
+        if out is None:
+            out = torch.empty((count, 32, 64), dtype=torch.float16, device=self._pool.device)
+        elif out.shape != (count, 32, 64) or out.dtype != torch.float16 or out.stride()[1:] != (64, 1):
+            raise ValueError("out must be FP16 [batch, 32, 64] with contiguous rows")
+        fixed = staged.launch_args
+        if fixed is None:
+            fixed = staged.launch_args = self._decode_layer_args(self.staged_decode_batch(), count)
+        pool_ptr, num_blocks, rope, lengths, prefix, flat, cta_rows, total, grid, per_cta, ws, ws_bytes, err, stream = fixed
+        check(
+            lib.pkv_decode_layer(
+                pool_ptr, num_blocks, layer, query.data_ptr(), query.stride(0), key.data_ptr(), value.data_ptr(),
+                key.stride(0), rope, lengths, prefix, flat, cta_rows, count, total, grid, per_cta, out.data_ptr(),
+                out.stride(0), ws, ws_bytes, err, stream,
+            )
         )
         self._ledger.decode_mark(-1, layer)
         staged.written = layer + 1
         return out
+
+    def _decode_layer_args(self, batch: DecodeBatch, count: int) -> tuple:
+        """Launch arguments of pkv_decode_layer that stay fixed for a staged step."""
+        workspace = self._workspace_for(batch.plan.workspace_bytes)
+        return (
+            self._pool.data_ptr(), self._pool.shape[2], self._rope.data_ptr(), batch.lengths.data_ptr(),
+            batch.prefix.data_ptr(), batch.flat.data_ptr(), batch.cta_rows.data_ptr(), batch.total_blocks,
+            batch.plan.grid, batch.plan.blocks_per_cta, 0 if workspace is None else workspace.data_ptr(),
+            0 if workspace is None else workspace.numel() * 4, self._error.data_ptr(), self._stream.cuda_stream,
+        )
 
     def staged_decode_batch(self) -> DecodeBatch:
         """Device tables of the staged batch with every row's new token included."""
@@ -493,13 +505,18 @@ class KVAllocator:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
         used = 2 * count + 1 + total
-        device = self._upload_i32(host[:used])
         plan = kernels.decode_plan(self._pool.device, count, total)
+        prefix = host[count : 2 * count + 1]
+        starts = np.arange(plan.grid, dtype=np.int64) * plan.blocks_per_cta
+        rows = np.searchsorted(prefix, starts, side="right") - 1
+        cta_rows = np.stack((rows, prefix[rows]), axis=1).astype(np.int32).reshape(-1)
+        device = self._upload_i32(host[:used], cta_rows)
         return DecodeBatch(
             requests=request_ids,
             lengths=device[:count],
             prefix=device[count : 2 * count + 1],
             flat=device[2 * count + 1 : used],
+            cta_rows=device[used:],
             total_blocks=total,
             plan=plan,
             host_lengths=host[:count].copy(),
@@ -522,5 +539,6 @@ class KVAllocator:
             out,
             self._workspace_for(batch.plan.workspace_bytes),
             self._error,
+            batch.cta_rows,
         )
         return out

@@ -43,7 +43,7 @@ def test_device_entry_points_reject_bad_arguments_before_any_launch() -> None:
     status = _lib.lib.pkv_append_kv(None, 1, 0, 1, None, None, 0, 0, None, None, 1, None, None, None, 0, 0, None, None)
     assert status == _lib.PKV_VALUE_ERROR
     status = _lib.lib.pkv_decode_attention(
-        None, 1, 0, None, 0, None, None, None, 1, 1, 1, 1, None, 0, None, 0, None, None
+        None, 1, 0, None, 0, None, None, None, None, 1, 1, 1, 1, None, 0, None, 0, None, None
     )
     assert status == _lib.PKV_VALUE_ERROR
     assert b"null pointer" in _lib.lib.pkv_last_error()

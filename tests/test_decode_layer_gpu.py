@@ -74,7 +74,6 @@ def test_fused_layer_matches_separate_path_bit_for_bit() -> None:
         assert torch.equal(fused_out[layer], separate_out[layer]), layer
     assert fused.capacity() == separate.capacity()
     assert [fused.cached_length(r) for r in requests] == [n + 1 for n in LENGTHS]
-    assert int(fused._counters.abs().sum()) == 0
 
 
 @pytest.mark.parametrize("blocks_per_cta", [1, 2, 3, 7, 16, 300])
@@ -91,18 +90,16 @@ def test_fused_layer_matches_oracle_under_every_plan(blocks_per_cta: int, rope_g
         grid = (batch.total_blocks + blocks_per_cta - 1) // blocks_per_cta
         plan = kernels.DecodePlan(grid, blocks_per_cta, (count + grid) * 32 * 66 * 4)
         workspace = torch.empty(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
-        counters = torch.zeros(count * 4, dtype=torch.int32, device=device)
         for layer in range(22):
             allocator.ledger.decode_check(-1, layer)
             out = torch.empty(count, 32, 64, dtype=torch.float16, device=device)
             kernels.decode_layer(allocator.pool, layer, q[layer], k[layer], v[layer], allocator._rope, batch.lengths,
-                                 batch.prefix, batch.flat, batch.total_blocks, plan, out, workspace, counters,
+                                 batch.prefix, batch.flat, batch.total_blocks, plan, out, workspace,
                                  allocator._error)
             allocator.ledger.decode_mark(-1, layer)
             outputs.append(out)
     torch.cuda.synchronize()
     allocator.check_device_errors()
-    assert int(counters.abs().sum()) == 0
 
     # Oracle: the same staged append on a copy of the pool, then the reference attention.
     oracle_pool = before.copy()
