@@ -220,6 +220,26 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
                      int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
                      void *stream);
 
+/* pkv_decode_attention without any allocation.  No counterpart in the
+ * reference: it is for callers that cannot allocate device memory for this
+ * library (a host whose device memory is all owned by another allocator, or a
+ * plugin host with no workspace callback).  Same arguments and result as
+ * pkv_decode_attention minus the workspace: the split partials live in one
+ * 8 MiB file-scope device array, which every GPU that loads the library holds
+ * until exit.  Limit: batch + grid <= 992, else PKV_VALUE_ERROR.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * and sets the kernel attributes with that device current; make that first
+ * call before any stream capture.  All calls share the array and it keeps the
+ * last call's contents (nothing in it needs to start at zero: every partial
+ * is written before it is read within one call), so calls that overlap on the
+ * GPU - on different streams, or on one device from different threads - race
+ * and must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
+int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                 int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
+                                 const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
+                                 int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
+                                 int32_t *error_flag, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

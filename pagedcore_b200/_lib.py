@@ -115,6 +115,28 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # stream
         ],
     ),
+    "pkv_decode_attention_noalloc": (
+        c_int,
+        [
+            c_void_p,  # pool
+            c_int32,  # num_blocks
+            c_int32,  # layer
+            c_void_p,  # query
+            c_int64,  # query_stride
+            c_void_p,  # lengths
+            c_void_p,  # prefix
+            c_void_p,  # flat
+            c_void_p,  # cta_rows
+            c_int32,  # batch
+            c_int32,  # total_blocks
+            c_int32,  # grid
+            c_int32,  # blocks_per_cta
+            c_void_p,  # out
+            c_int64,  # out_stride
+            c_void_p,  # error_flag
+            c_void_p,  # stream
+        ],
+    ),
     "pkv_decode_attention": (
         c_int,
         [

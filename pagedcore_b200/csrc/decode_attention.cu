@@ -876,3 +876,104 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
     return launch_pass<true>(grid, map, args, static_cast<cudaStream_t>(stream), "decode layer");
 }
+
+// ---------------------------------------------------------------------------
+// Decode attention without any allocation (pkv_decode_attention_noalloc).
+//
+// Some hosts cannot hand this library device memory for its split partials:
+// a serving process whose device memory is entirely owned by another
+// allocator (the KV pool reserved up front, no further cudaMalloc allowed),
+// or a plugin host that offers no workspace callback.  For them the partials
+// live in one file-scope device array of fixed size, and the host code below
+// reaches it through cudaGetSymbolAddress: in host code the array's name is
+// only a stand-in for the symbol, not a device address.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB, held by every device that loads the library
+constexpr int kNoAllocMaxSlots = static_cast<int>(kNoAllocScratchBytes / (kPartialFloats * sizeof(float)));  // 992
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchBytes / sizeof(float)];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_scratch[kNoAllocMaxDevices] = {};
+
+// Once per device, with that device current: the array's device address and
+// the kernels' shared-memory attribute.  Nothing here allocates.
+int noalloc_setup(int device, void **scratch) {
+    if (device < 0 || device >= kNoAllocMaxDevices) {
+        return pkv::fail(PKV_VALUE_ERROR, "no-alloc decode attention: device ordinal out of range");
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_scratch[device] == nullptr) {
+        void *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
+        if (e != cudaSuccess || ptr == nullptr) {
+            return pkv::fail(PKV_CUDA_ERROR, std::string("no-alloc decode attention: cudaGetSymbolAddress failed: ") +
+                                                 cudaGetErrorString(e));
+        }
+        const int stages = configured_stages();
+        e = stages == 4 ? cudaFuncSetAttribute(decode_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               smem_bytes<4>())
+            : stages == 8 ? cudaFuncSetAttribute(decode_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 smem_bytes<8>())
+                          : cudaFuncSetAttribute(decode_kernel<6, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 smem_bytes<6>());
+        if (e != cudaSuccess) {
+            return pkv::fail(PKV_CUDA_ERROR, std::string("no-alloc decode attention: cudaFuncSetAttribute: ") +
+                                                 cudaGetErrorString(e));
+        }
+        g_noalloc_scratch[device] = ptr;
+    }
+    *scratch = g_noalloc_scratch[device];
+    return PKV_OK;
+}
+
+// The pool's tensor map, encoded into a local value (no cache, no allocation).
+int noalloc_pool_map(const void *pool, int32_t num_blocks, CUtensorMap *map) {
+    EncodeTiled encode = encode_fn();
+    if (encode == nullptr) return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t rows = static_cast<cuuint64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(kKvHeads), rows};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kRowBytes), static_cast<cuuint64_t>(kKvHeads * kRowBytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHeadDim), 1u, static_cast<cuuint32_t>(kBlockTokens)};
+    const cuuint32_t elem[3] = {1u, 1u, 1u};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(pool), dims, strides, box,
+                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+    }
+    return PKV_OK;
+}
+
+}  // namespace
+
+extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                            int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
+                                            const int32_t *flat, const int32_t *cta_rows, int32_t batch,
+                                            int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
+                                            int64_t out_stride, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    if (static_cast<int64_t>(batch) + grid > kNoAllocMaxSlots) {
+        return pkv::fail(PKV_VALUE_ERROR,
+                         "no-alloc decode attention: batch + grid = " + std::to_string(int64_t(batch) + grid) +
+                             " exceeds the static scratch limit of " + std::to_string(kNoAllocMaxSlots) +
+                             " (8 MiB of split partials); use pkv_decode_attention with a workspace");
+    }
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    void *scratch = nullptr;
+    int rc = noalloc_setup(device, &scratch);
+    if (rc) return rc;
+    LayerArgs args;
+    rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+                       total_blocks, grid, blocks_per_cta, out, out_stride, scratch, kNoAllocScratchBytes,
+                       error_flag, &args);
+    if (rc) return rc;
+    CUtensorMap map;
+    if ((rc = noalloc_pool_map(pool, num_blocks, &map))) return rc;
+    return launch_pass<false>(grid, map, args, static_cast<cudaStream_t>(stream), "no-alloc decode attention");
+}

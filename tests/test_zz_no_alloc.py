@@ -1,0 +1,93 @@
+"""The allocation-free decode attention entry point, through the C ABI.
+
+``pkv_decode_attention_noalloc`` serves callers that cannot give this library
+device memory (their device memory belongs to another allocator, or their
+plugin interface has no workspace callback): it keeps its split partials in a
+fixed device array instead of a caller workspace.  It must return what
+``pkv_decode_attention`` returns for the same batch, also on a second call
+that finds the previous call's data still in that array.  The file is named to
+be collected last; it builds its own cache so it also runs alone.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from pagedcore_b200 import _lib, kernels, workloads
+from pagedcore_b200.engine_types import KVReservation, RequestId
+from pagedcore_b200.kv_cache import KVAllocator
+from tests.conftest import cuda_device
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(allocator: KVAllocator, batch, query: torch.Tensor, layer: int, out: torch.Tensor) -> int:
+    return _lib.lib.pkv_decode_attention_noalloc(
+        allocator.pool.data_ptr(),
+        allocator.pool.shape[2],
+        layer,
+        query.data_ptr(),
+        query.stride(0),
+        batch.lengths.data_ptr(),
+        batch.prefix.data_ptr(),
+        batch.flat.data_ptr(),
+        batch.cta_rows.data_ptr(),
+        len(batch.requests),
+        batch.total_blocks,
+        batch.plan.grid,
+        batch.plan.blocks_per_cta,
+        out.data_ptr(),
+        out.stride(0),
+        allocator._error.data_ptr(),
+        torch.cuda.current_stream().cuda_stream,
+    )
+
+
+def _cache(lengths: list[int], device: torch.device) -> tuple[KVAllocator, tuple[RequestId, ...]]:
+    need = sum(workloads.blocks_for(n) for n in lengths) + 4
+    pool = torch.full((22, 2, need, 16, 4, 64), torch.nan, dtype=torch.float16, device=device)
+    allocator = KVAllocator(pool, validation="incremental")
+    allocator.ledger.reorder_free(workloads.rng(41, 1).permutation(need).astype(np.int32))
+    generator = torch.Generator(device=device).manual_seed(41)
+    requests = []
+    for row, length in enumerate(lengths):
+        request = RequestId(f"n{row}")
+        allocator.create(KVReservation(request, workloads.blocks_for(length)))
+        key = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+        value = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+        allocator.append(request, key, value)
+        requests.append(request)
+    return allocator, tuple(requests)
+
+
+def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row() -> None:
+    device = cuda_device()
+    lengths = workloads.decode_lengths(43, 64, high=2048).tolist()
+    allocator, requests = _cache(lengths, device)
+    generator = torch.Generator(device=device).manual_seed(43)
+    for layer in (3, 17):  # the second call finds the first call's partials in the array
+        batch = allocator.decode_batch(requests, layer_index=layer)
+        assert batch.plan.grid > 1  # rows are split, so the partials array is used
+        query = torch.randn(len(lengths), 32, 64, dtype=torch.float16, device=device, generator=generator)
+        expected = torch.empty_like(query)
+        kernels.decode_attention(allocator.pool, layer, query, batch.lengths, batch.prefix, batch.flat,
+                                 batch.total_blocks, batch.plan, expected,
+                                 allocator._workspace_for(batch.plan.workspace_bytes), allocator._error,
+                                 batch.cta_rows)
+        actual = torch.full_like(query, float("nan"))
+        assert _noalloc(allocator, batch, query, layer, actual) == _lib.PKV_OK, _lib.lib.pkv_last_error()
+        torch.cuda.synchronize()
+        allocator.check_device_errors()
+        torch.testing.assert_close(actual, expected, atol=2e-3, rtol=1e-2)
+
+
+def test_noalloc_entry_rejects_batches_beyond_its_fixed_array() -> None:
+    # Refused on the host before any launch: batch + grid must not exceed 992.
+    cuda_device()
+    status = _lib.lib.pkv_decode_attention_noalloc(
+        None, 1, 0, None, 0, None, None, None, None, 990, 1000, 10, 100, None, 0, None, None
+    )
+    assert status == _lib.PKV_VALUE_ERROR
+    assert b"exceeds the static scratch limit of 992" in _lib.lib.pkv_last_error()
