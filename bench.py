@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -184,58 +183,83 @@ def _traffic_per_launch() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+    """SM clock and throttle-reason samples (NVML, read-only) every 10 ms of the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits.
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, devices: list[int]) -> None:
-        self.devices = devices
-        self.proc = None
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self, pynvml):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.device)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            domain = getattr(props, "pci_domain_id", 0)
+            slot = getattr(props, "pci_device_id", 0)
+            try:
+                return pynvml.nvmlDeviceGetHandleByPciBusId(f"{domain:08x}:{bus:02x}:{slot:02x}.0")
+            except pynvml.NVMLError:
+                pass
+        return pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def __enter__(self) -> "ClockSampler":
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", ",".join(str(d) for d in self.devices)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = self._handle(pynvml)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        except Exception as error:  # noqa: BLE001 - clocks are reported, never required
+            self.error = f"NVML unavailable: {error}"
+            return self
+        self._stop = threading.Event()
+
+        def run() -> None:
+            while not self._stop.is_set():
+                try:
+                    mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                    reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
+                    self.samples.append((mhz, reasons))
+                except Exception as error:  # noqa: BLE001
+                    self.error = str(error)
+                    return
+                self._stop.wait(0.01)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc) -> None:
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.output, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.output, _ = self.proc.communicate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        clocks, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (self.output or "").splitlines():
-            fields = [f.strip() for f in line.split(",")]
-            if len(fields) < 9:
-                continue
-            try:
-                clocks.append(float(fields[1]))
-                maxes.append(float(fields[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, fields[5:9]):
-                if flag.lower() == "active":
+        reasons = set()
+        for _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        return {
-            "sm_mhz": statistics.median(clocks) if clocks else None,
-            "sm_max_mhz": max(maxes) if maxes else None,
-            "samples": len(clocks),
+        summary = {
+            "sm_mhz": statistics.median(mhz for mhz, _ in self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples),
             "reasons": sorted(reasons),
+            "source": "NVML every 10 ms during the timed region",
         }
+        if self.error:
+            summary["error"] = self.error
+        return summary
 
 
 def run_gpu_arm(args: argparse.Namespace) -> None:
@@ -343,7 +367,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                    for _ in range(args.steps)]
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler([local_rank]) as clocks:
+    with ClockSampler(local_rank) as clocks:
         torch.cuda.nvtx.range_push("timed")
         start.record(stream)
         for i in range(args.steps):
@@ -434,15 +458,18 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            sample_rows = [int(n) for n in case.lengths[:4]]
-            seconds = oracle_decode_rows(sample_rows, case.num_blocks, steps=2, warmup=0, seed=seed)
+            from threadpoolctl import threadpool_limits
+
+            sample_rows = [int(n) for n in case.lengths[:48]]
+            with threadpool_limits(1):
+                seconds = oracle_decode_rows(sample_rows, case.num_blocks, steps=2, warmup=0, seed=seed)
             line["cpu_baseline"] = {
                 "value": len(sample_rows) * 2 / seconds,
                 "unit": "tokens/s",
                 "cores": 1,
                 "kind": "port",
-                "sample": f"{len(sample_rows)} rows x 2 decode steps x 22 layers of the same workload, single "
-                          f"thread, oracle restatement of the reference CPU path ({seconds:.1f}s)",
+                "sample": f"{len(sample_rows)} of the {SEQUENCES} rows x 2 decode steps x 22 layers of the same "
+                          f"workload, one thread, oracle restatement of the reference CPU path ({seconds:.1f}s)",
             }
         print(json.dumps(line), flush=True)
     if world > 1:
