@@ -1,7 +1,7 @@
 """Benchmark of the paged KV-cache hot path on B200.
 
 One step = one batched one-token decode step of the KV path over all 22
-layers for the rank's 256 sequences (contexts U[1, 2048-64], tables
+layers for the rank's 256 sequences (contexts U[1, 2048 - room for the run's appends], tables
 fragmented by allocator churn): staged append in the C++ ledger, then per
 layer the fused K/Q-RoPE + KV scatter kernel and the split-K GQA decode
 attention (+ combine), then the commit.  The dense TinyLlama GEMMs around it
@@ -150,8 +150,8 @@ def run_reference_arm(args: argparse.Namespace) -> None:
 # ---------------------------------------------------------------------------
 def _config(n_gpus: int) -> dict:
     return {
-        "workload": "BASELINE config 4, KV hot path: 256 sequences per GPU, contexts U[1, 1984], churned "
-                    "block tables; one step = staged append + 22 fused decode-layer launches (Q/K RoPE, "
+        "workload": "BASELINE config 4, KV hot path: 256 sequences per GPU, contexts U[1, 2048 - room for the "
+                    "run's appends], churned block tables; one step = staged append + 22 fused decode-layer launches (Q/K RoPE, "
                     "new-token KV write, split-K GQA decode attention) + commit; dense GEMMs not included",
         "sequences_per_gpu": SEQUENCES,
         "layers": LAYERS,
@@ -171,19 +171,19 @@ def _peak_hbm() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def _traffic_per_launch() -> float | None:
-    """DRAM bytes per attention launch from the committed ncu summary, if any."""
-    path = ROOT / "profiles" / "decode_attention_cfg4.md"
+def _traffic_ratio() -> float | None:
+    """ncu DRAM bytes per decode-layer launch / algorithmic bytes, from the committed summary."""
+    path = ROOT / "profiles" / "decode_layer_cfg4.md"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith("traffic_per_algorithmic_byte:"):
             return float(line.split(":", 1)[1].strip())
     return None
 
 
 class ClockSampler:
-    """SM clock and throttle-reason samples (NVML, read-only) every 10 ms of the timed region."""
+    """SM clock and throttle-reason samples (NVML, read-only) every 2 ms of the timed region."""
 
     # NVML clock-event reason bits.
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
@@ -233,7 +233,7 @@ class ClockSampler:
                 except Exception as error:  # noqa: BLE001
                     self.error = str(error)
                     return
-                self._stop.wait(0.01)
+                self._stop.wait(0.002)
 
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
@@ -255,7 +255,7 @@ class ClockSampler:
             "sm_max_mhz": self.max_mhz,
             "samples": len(self.samples),
             "reasons": sorted(reasons),
-            "source": "NVML every 10 ms during the timed region",
+            "source": "NVML every 2 ms during the timed region",
         }
         if self.error:
             summary["error"] = self.error
@@ -285,7 +285,10 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
 
     total_steps = args.warmup + args.steps
     seed = 4 + 1000 * rank
-    case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=2 * total_steps)
+    # Room for every append of the run: warm-up, plan, timed, e2e warm-up and e2e steps.
+    room = 2 * total_steps + 4
+    case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=room)
+    context_high = 2048 - room
     pool = torch.empty((22, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
     allocator = KVAllocator(pool, validation="incremental")
 
@@ -318,12 +321,13 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     out = torch.empty(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device)
     stream = torch.cuda.current_stream(device)
 
-    def step(q, k, v, attn_events=None) -> None:
+    def step(q, k, v, attn_events=None, dst=None) -> None:
+        dst = out if dst is None else dst
         with allocator.append_decode(requests):
             for layer in range(LAYERS):
                 if attn_events is not None:
                     attn_events[layer][0].record(stream)
-                allocator.decode_layer(layer, q[layer], k[layer], v[layer], out=out[layer])
+                allocator.decode_layer(layer, q[layer], k[layer], v[layer], out=dst[layer])
                 if attn_events is not None:
                     attn_events[layer][1].record(stream)
 
@@ -336,12 +340,12 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         step(*device_inputs[i % 2])
     allocator.check_device_errors()
 
-    # Algorithmic bytes of one fused decode-layer launch, from the plan of the
-    # staged batch: K/V streamed (1024 B per cached token, the new one
-    # included), block-table entries, Q in / attention out (4 KiB each), the
-    # new token's K/V in (1 KiB) and written to the pool (1 KiB), lengths and
-    # prefix, and the split partials written then read back (32 heads x 66 FP32
-    # per segment of a split row).
+    # Algorithmic bytes of one fused decode-layer launch, from the staged
+    # batch: K/V streamed (1024 B per cached token, the new one included),
+    # block-table entries, Q in / attention out (4 KiB each), the new token's
+    # K/V in (1 KiB) and written to the pool (1 KiB), lengths and prefix.  The
+    # split partials are not counted: they are a by-product of the split, not
+    # bytes the operation needs.
     plan_info = {}
 
     def layer_bytes() -> float:
@@ -349,15 +353,12 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             batch = allocator.staged_decode_batch()
             for layer in range(LAYERS):
                 allocator.decode_layer(layer, *(x[layer] for x in device_inputs[0]), out=out[layer])
-        plan_info.update(grid=batch.plan.grid, blocks_per_cta=batch.plan.blocks_per_cta,
-                         total_blocks=batch.total_blocks)
+        big, tail = batch.plan.pieces()
+        plan_info.update(grid=batch.plan.grid, blocks_per_cta=batch.plan.blocks_per_cta, big_ctas=big,
+                         tail_blocks=tail, total_blocks=batch.total_blocks)
         lengths = batch.host_lengths.astype(np.int64)
-        plan = batch.plan
         blocks = (lengths + 15) // 16
-        prefix = np.concatenate([[0], np.cumsum(blocks)])
-        segments = (prefix[1:] - 1) // plan.blocks_per_cta - prefix[:-1] // plan.blocks_per_cta + 1
         per_row = 1024 * lengths + 4 * blocks + 2 * 4096 + 2 * 1024 + 8
-        per_row = per_row + np.where(segments > 1, segments * 32 * 66 * 4 * 2, 0)
         return float(per_row.sum())
 
     # One extra staged step (its tokens are real appends) measures the plan.
@@ -379,25 +380,55 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     layer_ms = sum(a.elapsed_time(b) for per_step in attn_events for a, b in per_step)
     allocator.check_device_errors()
 
-    # End to end through the public API with host buffers.
+    # End to end through the public API with host buffers: every step copies
+    # its Q/K/V in from pinned host memory and its attention outputs back out.
+    # The copies run on two copy streams, double-buffered by step, so step
+    # i+1's inputs load and step i's outputs drain while layers compute.
     host_inputs = [tuple(t.cpu().pin_memory() for t in device_inputs[i]) for i in range(2)]
-    staging = [torch.empty_like(t) for t in device_inputs[0]]
-    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    staging = [[torch.empty_like(t) for t in device_inputs[0]] for _ in range(2)]
+    outs = [torch.empty_like(out) for _ in range(2)]
+    host_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
     h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs[0])
-    d2h_bytes = host_out.numel() * host_out.element_size()
-    for i in range(2):
-        for dst, src in zip(staging, host_inputs[i]):
-            dst.copy_(src, non_blocking=True)
-        step(*staging)
-        host_out.copy_(out, non_blocking=True)
+    d2h_bytes = host_out[0].numel() * host_out[0].element_size()
+    copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def e2e_steps(count: int) -> None:
+        loaded = [torch.cuda.Event() for _ in range(2)]    # staging[b] holds its step's inputs
+        consumed = [torch.cuda.Event() for _ in range(2)]  # the step reading staging[b] is done
+        computed = [torch.cuda.Event() for _ in range(2)]  # outs[b] holds its step's outputs
+        drained = [torch.cuda.Event() for _ in range(2)]   # outs[b] is copied out
+
+        def load(i: int) -> None:
+            b = i % 2
+            copy_in.wait_event(consumed[b])
+            with torch.cuda.stream(copy_in):
+                for dst, src in zip(staging[b], host_inputs[i % 2]):
+                    dst.copy_(src, non_blocking=True)
+            loaded[b].record(copy_in)
+
+        copy_in.wait_stream(stream)  # the first copy starts after the timer does
+        load(0)
+        for i in range(count):
+            b = i % 2
+            if i + 1 < count:
+                load(i + 1)
+            stream.wait_event(loaded[b])
+            stream.wait_event(drained[b])
+            step(*staging[b], dst=outs[b])
+            consumed[b].record(stream)
+            computed[b].record(stream)
+            copy_out.wait_event(computed[b])
+            with torch.cuda.stream(copy_out):
+                host_out[b].copy_(outs[b], non_blocking=True)
+            drained[b].record(copy_out)
+        for b in range(2):
+            stream.wait_event(drained[b])
+
+    e2e_steps(2)
     barrier()
     e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_start.record(stream)
-    for i in range(args.steps):
-        for dst, src in zip(staging, host_inputs[i % 2]):
-            dst.copy_(src, non_blocking=True)
-        step(*staging)
-        host_out.copy_(out, non_blocking=True)
+    e2e_steps(args.steps)
     e2e_end.record(stream)
     barrier()
     e2e_ms = e2e_start.elapsed_time(e2e_end)
@@ -414,8 +445,9 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         peak, peak_kind = _peak_hbm()
         launch_ms = layer_ms / (args.steps * LAYERS)
         achieved = layer_bytes_per_launch / (launch_ms / 1000.0) / 1e9
-        traffic = _traffic_per_launch()
-        launches_per_step = LAYERS
+        ratio = _traffic_ratio()
+        traffic = None if ratio is None else ratio * layer_bytes_per_launch
+        launches_per_step = LAYERS * (2 if plan_info["grid"] > 1 else 1)  # split + combine
         line = {
             "metric": METRIC,
             "value": value,
@@ -428,14 +460,15 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "f16",
-            "data": "synthetic (seeded K/V/Q ~N(0,1), contexts U[1, 1984]); the reference publishes no inputs",
+            "data": f"synthetic (seeded K/V/Q ~N(0,1), contexts U[1, {context_high}]); the reference publishes "
+                    "no inputs",
             "config": _config(world),
             "attn_hbm_gbs": achieved,
             "attn_frac_of_peak": achieved / peak,
             "roofline": {
                 "bound": "hbm",
-                "kernel": "fused decode layer (decode_kernel<6,true>: Q/K RoPE, new-token KV write, split-K "
-                          "GQA attention, in-kernel merge), one launch per layer",
+                "kernel": "fused decode layer: decode_kernel<4,true> (Q/K RoPE, new-token KV write, split-K GQA "
+                          "attention) + decode_combine_kernel (programmatic dependent launch), per layer",
                 "achieved": achieved,
                 "peak": peak,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
@@ -445,14 +478,18 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                 "plan": plan_info,
                 "avg_launch_ms": launch_ms,
                 "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of decode_kernel per launch "
+                                  "over algorithmic bytes (profiles/decode_layer_cfg4.md), times this run's "
+                                  "algorithmic bytes",
             },
             "e2e": {
                 "value": tokens / (e2e_ms / 1000.0),
                 "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": d2h_bytes,
-                "path": "pinned host Q/K/V -> device, KVAllocator.write_decode_batch + paged_decode_attention, "
-                        "attention outputs -> pinned host, every step",
+                "path": "pinned host Q/K/V -> device and attention outputs -> pinned host every step, on two "
+                        "copy streams overlapped with the neighbouring steps; KVAllocator.append_decode + "
+                        "decode_layer per layer",
             },
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
@@ -460,7 +497,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         if world == 1 and not args.no_cpu_baseline:
             from threadpoolctl import threadpool_limits
 
-            sample_rows = [int(n) for n in case.lengths[:48]]
+            sample_rows = [int(n) for n in case.lengths[:192]]  # about 10 s of one core
             with threadpool_limits(1):
                 seconds = oracle_decode_rows(sample_rows, case.num_blocks, steps=2, warmup=0, seed=seed)
             line["cpu_baseline"] = {

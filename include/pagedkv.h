@@ -178,10 +178,14 @@ int pkv_append_kv(void *pool, int32_t num_blocks, int32_t layer_begin, int32_t l
                   void *stream);
 
 /* Launch plan of the split-K decode attention for `total_blocks` 16-token
- * blocks of a batch of `batch` sequences on `device`: grid size, blocks per
- * CTA, and the bytes of split partials the caller must provide as workspace. */
+ * blocks of a batch of `batch` sequences on `device`.  The flat block list is
+ * cut into one contiguous piece per CTA: big_ctas pieces of blocks_per_cta
+ * blocks, then grid - big_ctas pieces of tail_blocks blocks (the last piece
+ * may be shorter); big_ctas == grid is the uniform split.  Also returns the
+ * bytes of split partials the caller must provide as workspace. */
 int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
-                    int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes);
+                    int32_t *out_blocks_per_cta, int32_t *out_big_ctas, int32_t *out_tail_blocks,
+                    int64_t *out_workspace_bytes);
 
 /* Batched one-token block-table decode attention with GQA (8 query heads per
  * KV head).  Replaces paged_attention (attention.py:14-53) for a whole batch:
@@ -190,17 +194,19 @@ int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t
  * accumulation, one FP16 rounding.  query: FP16 [batch][32][64] with row
  * stride query_stride (elements); out likewise with out_stride.
  * lengths[batch], prefix[batch+1] (prefix[0] == 0), flat[total_blocks]:
- * int32 device arrays as written by pkv_ledger_batch.  grid / blocks_per_cta
- * / workspace come from pkv_decode_plan for the same (batch, total_blocks).
- * cta_rows (nullable): int32 [grid][2], for CTA g the row containing global
- * block g*blocks_per_cta and that row's first block prefix[row]; without it
- * every CTA searches prefix.  Two launches: the split kernel and, when
+ * int32 device arrays as written by pkv_ledger_batch.  grid / blocks_per_cta /
+ * big_ctas / tail_blocks / workspace come from pkv_decode_plan for the same
+ * (batch, total_blocks), or describe another partition that covers the
+ * blocks exactly.  cta_rows (nullable): int32 [grid][2], for CTA g the row
+ * containing the first block of its piece and that row's first block
+ * prefix[row]; without it every CTA searches prefix.  Two launches: the split kernel and, when
  * grid > 1, the combine kernel as its programmatic dependent. */
 int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                          int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
                          const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                         int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride, void *workspace,
-                         int64_t workspace_bytes, int32_t *error_flag, void *stream);
+                         int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks, void *out,
+                         int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
+                         void *stream);
 
 /* One decode layer for a staged batch: the fused form of write_decode_layer
  * (kv_cache.py:221-246) + apply_rope on Q and K (dense.py:33-61) +
@@ -216,9 +222,9 @@ int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, co
 int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
                      const void *key, const void *value, int64_t kv_stride, const void *rope_table,
                      const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
-                     int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
-                     int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
-                     void *stream);
+                     int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
+                     int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
+                     int32_t *error_flag, void *stream);
 
 /* pkv_decode_attention without any allocation.  No counterpart in the
  * reference: it is for callers that cannot allocate device memory for this
@@ -226,7 +232,8 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
  * plugin host with no workspace callback).  Same arguments and result as
  * pkv_decode_attention minus the workspace: the split partials live in one
  * 8 MiB file-scope device array, which every GPU that loads the library holds
- * until exit.  Limit: batch + grid <= 992, else PKV_VALUE_ERROR.  The first
+ * until exit.  Limit: the plan's workspace_bytes (pkv_decode_plan) must not
+ * exceed 8 MiB (batch + grid up to about 990), else PKV_VALUE_ERROR.  The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress)
  * and sets the kernel attributes with that device current; make that first
  * call before any stream capture.  All calls share the array and it keeps the
@@ -237,8 +244,8 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
 int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                  int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
                                  const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                                 int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
-                                 int32_t *error_flag, void *stream);
+                                 int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks,
+                                 void *out, int64_t out_stride, int32_t *error_flag, void *stream);
 
 #ifdef __cplusplus
 }

@@ -86,7 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,
         ],
     ),
-    "pkv_decode_plan": (c_int, [c_int32, c_int32, c_int32, i32p, i32p, i64p]),
+    "pkv_decode_plan": (c_int, [c_int32, c_int32, c_int32, i32p, i32p, i32p, i32p, i64p]),
     "pkv_decode_layer": (
         c_int,
         [
@@ -107,6 +107,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int32,  # total_blocks
             c_int32,  # grid
             c_int32,  # blocks_per_cta
+            c_int32,  # big_ctas
+            c_int32,  # tail_blocks
             c_void_p,  # out
             c_int64,  # out_stride
             c_void_p,  # workspace
@@ -131,6 +133,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int32,  # total_blocks
             c_int32,  # grid
             c_int32,  # blocks_per_cta
+            c_int32,  # big_ctas
+            c_int32,  # tail_blocks
             c_void_p,  # out
             c_int64,  # out_stride
             c_void_p,  # error_flag
@@ -153,6 +157,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_int32,  # total_blocks
             c_int32,  # grid
             c_int32,  # blocks_per_cta
+            c_int32,  # big_ctas
+            c_int32,  # tail_blocks
             c_void_p,  # out
             c_int64,  # out_stride
             c_void_p,  # workspace

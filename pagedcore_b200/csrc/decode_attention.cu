@@ -7,16 +7,21 @@
 //
 // Work split - balanced split-K over the batch's 16-token blocks.  The batch's
 // block tables are concatenated into one flat list (flat[prefix[b] + j] =
-// physical block of logical block j of row b); CTA g owns the contiguous
-// global block range [g*W, (g+1)*W), which may cover the tail of one row,
-// whole short rows and the head of another, so every CTA streams the same
-// number of KV bytes whatever the ragged lengths.  Warp w of a CTA serves KV
-// head w and its 8 query heads (GQA).
+// physical block of logical block j of row b); CTA g owns one contiguous
+// piece of it (the plan's Partition: normally [g*W, (g+1)*W)), which may
+// cover the tail of one row, whole short rows and the head of another, so
+// every CTA streams the same number of KV bytes whatever the ragged lengths.
+// Warp w of a CTA serves KV head w and its 8 query heads (GQA).
 //
 // Data movement - each warp runs its own TMA pipeline of STAGES stages: per
 // block, two 2 KiB boxes (the 16 K rows and 16 V rows of its head, 128 B
 // each, 512 B apart in the pool) land in shared memory with the 128-byte
-// swizzle, so ldmatrix reads are bank-conflict free.  Waits are bounded.
+// swizzle, so ldmatrix reads are bank-conflict free; the boxes carry an L2
+// evict-first policy (the KV stream is read once).  The piece's block ids
+// are held in registers 32 at a time and row boundaries come from a register
+// window of 32 rows, so no refill waits on a global load; each row's Q, RoPE
+// pairs and new token are prefetched into L2 when the CTA starts.  Waits are
+// bounded.
 //
 // Math - tensor-core tiles (mma.sync m16n8k16, FP16 in, FP32 accumulate):
 //   S^T[16 tok x 8 heads]  = K[16 x 64] . Q^T[64 x 8]         (4 MMAs)
@@ -34,14 +39,12 @@
 // Split rows - a row inside one CTA is normalised and written as FP16
 // directly.  A row split across CTAs leaves (m, l, O) partials at index
 // row + cta (unique: along the CTA order the (row, cta) pairs form a
-// monotone staircase, so row + cta strictly increases).  Two variants merge
-// them:
-//   * two-pass (paged_attention's drop-in path): decode_combine_kernel runs
-//     after the split kernel;
-//   * fused decode layer: the last warp to finish a (row, KV head) - counted
-//     with one atomic per warp, no waiting - merges the partials itself.  Only
-//     the first and last segments of a CTA's range can be split, so each warp
-//     publishes at most two partials, after its whole range is streamed.
+// monotone staircase, so row + cta strictly increases), and
+// decode_combine_kernel merges them, launched as a programmatic dependent of
+// the split kernel so its launch overlaps the split kernel's tail.  (A merge
+// inside the split kernel by the last piece of each row, counted with
+// atomics, measured 1.5 us per layer slower: it puts a merge on the tail of
+// every CTA.)
 //
 // The fused decode-layer variant also does the layer's KV append: it applies
 // RoPE to Q (every CTA of the row, in registers) and to the new token's K
@@ -101,7 +104,9 @@ struct LayerArgs {
     const int32_t *flat;       // [total_blocks]
     int32_t batch;
     int32_t total_blocks;
-    int32_t blocks_per_cta;
+    int32_t blocks_per_cta;    // size of the big pieces
+    int32_t big_ctas;          // number of big pieces
+    int32_t tail_blocks;       // size of the tail pieces
     int32_t num_blocks;
     int32_t layer;
     __half *out;               // [B][32][64], rows out_stride apart
@@ -111,6 +116,35 @@ struct LayerArgs {
     const int32_t *cta_rows;   // [grid][2]: first row of each CTA's range and its first block (or null)
     int32_t *error_flag;
 };
+
+// The plan's partition of the flat block list into one contiguous piece per
+// CTA: `big` pieces of `per_cta` blocks, then pieces of `tail` blocks.  The
+// tail pieces are later CTAs of the grid; the hardware starts each on
+// whichever SM frees a slot first, so SMs that stream faster take more of
+// them and all SMs finish together.  big == grid is the uniform partition.
+struct Partition {
+    int32_t total;
+    int32_t per_cta;
+    int32_t big;
+    int32_t tail;
+};
+
+__host__ __device__ __forceinline__ void piece_range(const Partition &p, int piece, int &begin, int &end) {
+    if (piece < p.big) {
+        begin = piece * p.per_cta;
+        end = begin + p.per_cta;
+    } else {
+        begin = p.big * p.per_cta + (piece - p.big) * p.tail;
+        end = begin + p.tail;
+    }
+    if (end > p.total) end = p.total;
+}
+
+// The piece holding global block `block`.
+__host__ __device__ __forceinline__ int piece_of(const Partition &p, int block) {
+    const int split = p.big * p.per_cta;
+    return block < split ? block / p.per_cta : p.big + (block - split) / p.tail;
+}
 
 __device__ __forceinline__ float warp_max8(float v) {
     // Reduce over the 8 lanes that share lane % 4 (the token rows of a fragment).
@@ -148,18 +182,21 @@ __device__ __forceinline__ uint32_t rope_half2(uint32_t x, uint32_t rot, bool ne
 
 __device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
-// One step of the split-partial merge, in a fixed operation order shared by
-// the fused kernel and the two-pass combine kernel (so both give the same
-// bits): fold partial (m, l, o0, o1) into the running (M, L, A0, A1).
-__device__ __forceinline__ void merge_partial(float &M, float &L, float &A0, float &A1, float m, float l, float o0,
-                                              float o1) {
+// One step of the split-partial merge, in a fixed operation order: the running (M, L, A) of a head absorbs a partial (m, l, o) as
+//   M' = max(M, m),  L' = L a + l b,  A' = A a + o b,  a = 2^(M - M'),  b = 2^(m - M').
+struct MergeWeights {
+    float a, b;
+};
+
+__device__ __forceinline__ MergeWeights merge_weights(float &M, float m) {
     const float mn = fmaxf(M, m);
-    const float a = pkv::exp2_approx(M - mn);
-    const float b = pkv::exp2_approx(m - mn);
-    L = __fmaf_rn(L, a, __fmul_rn(l, b));
-    A0 = __fmaf_rn(A0, a, __fmul_rn(o0, b));
-    A1 = __fmaf_rn(A1, a, __fmul_rn(o1, b));
+    const MergeWeights w{pkv::exp2_approx(M - mn), pkv::exp2_approx(m - mn)};
     M = mn;
+    return w;
+}
+
+__device__ __forceinline__ float merge_value(float A, float o, MergeWeights w) {
+    return __fmaf_rn(A, w.a, __fmul_rn(o, w.b));
 }
 
 // Fetch one block's K and V boxes of KV head `head` into a pipeline stage
@@ -167,7 +204,8 @@ __device__ __forceinline__ void merge_partial(float &M, float &L, float &A0, flo
 // completes the stage's phase without data, so no waiter is left behind.
 __device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t block, int32_t num_blocks,
                                             int32_t k_rows, int32_t v_rows, int head, uint32_t dst,
-                                            uint32_t bar, int32_t *error_flag, uint32_t after = 0u) {
+                                            uint32_t bar, int32_t *error_flag, uint64_t policy,
+                                            uint32_t after = 0u) {
     // `after` ties the issue to a value computed from the stage's last reads.
     asm volatile("" ::"r"(after) : "memory");
     if (block < 0 || block >= num_blocks) {
@@ -176,16 +214,26 @@ __device__ __forceinline__ void issue_block(const CUtensorMap *map, int32_t bloc
         return;
     }
     pkv::mbar_arrive_expect_tx(bar, kStageBytes);
-    pkv::tma_load_3d(dst, map, 0, head, k_rows + block * kBlockTokens, bar);
-    pkv::tma_load_3d(dst + kTileBytes, map, 0, head, v_rows + block * kBlockTokens, bar);
+    pkv::tma_load_3d_hint(dst, map, 0, head, k_rows + block * kBlockTokens, bar, policy);
+    pkv::tma_load_3d_hint(dst + kTileBytes, map, 0, head, v_rows + block * kBlockTokens, bar, policy);
 }
 
-// Per-row inputs of a segment.  The head (two int32) is loaded two rows
-// ahead, the body one row ahead, so that row switches never wait on
-// global-memory latency behind the KV stream.
+// Per-row inputs of a segment.  The head (where the row ends in the flat
+// list, and its length) comes from a row window held in registers; the body
+// (Q fragments, RoPE pairs, the new token) is loaded one row ahead, from L2:
+// the kernel prefetches the bodies of its range's rows into L2 at its start,
+// so row switches do not wait on DRAM latency behind the KV stream.
 struct RowHead {
     int32_t last;    // prefix[row + 1]
     int32_t length;  // lengths[row]
+};
+
+// Lane j holds prefix[base + j + 1] and lengths[base + j]: the heads of rows
+// base .. base + 31, read by shuffle.
+struct RowWindow {
+    int32_t base;
+    int32_t last;
+    int32_t length;
 };
 
 struct RowBody {
@@ -196,10 +244,20 @@ struct RowBody {
     int32_t last_block;    // FUSED: flat[last - 1]
 };
 
-__device__ __forceinline__ RowHead row_head(const LayerArgs &a, int row) {
+__device__ __forceinline__ RowWindow load_row_window(const LayerArgs &a, int base, int lane) {
+    RowWindow w;
+    w.base = base;
+    const int r = base + lane;
+    w.last = r < a.batch ? a.prefix[r + 1] : INT32_MAX;
+    w.length = r < a.batch ? a.lengths[r] : 0;
+    return w;
+}
+
+// Head of `row` (warp-uniform, base <= row < base + 32).
+__device__ __forceinline__ RowHead window_head(const RowWindow &w, int row) {
     RowHead h;
-    h.last = a.prefix[row + 1];
-    h.length = a.lengths[row];
+    h.last = __shfl_sync(0xffffffffu, w.last, row - w.base);
+    h.length = __shfl_sync(0xffffffffu, w.length, row - w.base);
     return h;
 }
 
@@ -210,6 +268,37 @@ __device__ __forceinline__ int clamp_position(const LayerArgs &a, int length, in
         pos = 0;
     }
     return pos;
+}
+
+// Prefetch into L2 the lines row_body will read for `row` and KV head `warp`.
+template <bool FUSED>
+__device__ __forceinline__ void prefetch_row(const LayerArgs &a, int row, int length, int last, int warp) {
+    const char *q = reinterpret_cast<const char *>(a.query + row * a.query_stride + warp * kGroup * kHeadDim);
+#pragma unroll
+    for (int offset = 0; offset < kGroup * kRowBytes; offset += 128) pkv::prefetch_l2(q + offset);
+    pkv::prefetch_l2(q + kGroup * kRowBytes - 1);
+    if constexpr (FUSED) {
+        const __half *kn = a.key_new + row * a.new_stride + warp * kHeadDim;
+        const __half *vn = a.value_new + row * a.new_stride + warp * kHeadDim;
+        pkv::prefetch_l2(kn);
+        pkv::prefetch_l2(kn + kHeadDim - 1);
+        pkv::prefetch_l2(vn);
+        pkv::prefetch_l2(vn + kHeadDim - 1);
+        const int pos = length >= 1 && length <= PKV_CONTEXT_LIMIT ? length - 1 : 0;
+        pkv::prefetch_l2(a.rope_cos + pos * kRopeHalf);
+        pkv::prefetch_l2(a.rope_cos + pos * kRopeHalf + kRopeHalf - 1);
+        pkv::prefetch_l2(a.rope_sin + pos * kRopeHalf);
+        pkv::prefetch_l2(a.rope_sin + pos * kRopeHalf + kRopeHalf - 1);
+        if (last >= 1 && last <= a.total_blocks) pkv::prefetch_l2(a.flat + last - 1);
+    }
+}
+
+// Lane j >= 1 prefetches the body of window row base + j if that row starts
+// inside [.., end) (row base is loaded directly).
+template <bool FUSED>
+__device__ __forceinline__ void prefetch_window(const LayerArgs &a, const RowWindow &w, int end, int lane, int warp) {
+    const int start = __shfl_up_sync(0xffffffffu, w.last, 1);  // prefix[base + lane]
+    if (lane >= 1 && w.base + lane < a.batch && start < end) prefetch_row<FUSED>(a, w.base + lane, w.length, w.last, warp);
 }
 
 template <bool FUSED>
@@ -243,18 +332,54 @@ __device__ __forceinline__ void row_body(const LayerArgs &a, int row, const RowH
         m.k_own = ld32(kn + d);
         m.k_partner = ld32(kn + ((d + kRopeHalf) & (kHeadDim - 1)));
         m.v_own = ld32(a.value_new + row * a.new_stride + warp * kHeadDim + d);
-        m.last_block = a.flat[h.last - 1];
+        m.last_block = h.last >= 1 && h.last <= a.total_blocks ? a.flat[h.last - 1] : -1;
     }
 }
 
+// Write this warp's (m, l, O) of its 8 heads to partial slot `index`.  In the
+// MMA fragment layout lane (g, t) holds heads head0 = 8*warp + 2t and
+// head0 + 1, dims 16*mt + g and 16*mt + g + 8 (o[mt][0|2] for head0,
+// o[mt][1|3] for head0 + 1).
+__device__ __forceinline__ void store_partial(const LayerArgs &a, int64_t index, int head0, int g,
+                                              const float (&o)[4][4], float m0, float l0, float m1, float l1) {
+    float *po = a.part_o + index * kQueryHeads * kHeadDim;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        const int d = 16 * mt + g;
+        po[head0 * kHeadDim + d] = o[mt][0];
+        po[(head0 + 1) * kHeadDim + d] = o[mt][1];
+        po[head0 * kHeadDim + d + 8] = o[mt][2];
+        po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
+    }
+    if (g == 0) {
+        *reinterpret_cast<float4 *>(a.part_ml + index * kQueryHeads * 2 + head0 * 2) = make_float4(m0, l0, m1, l1);
+    }
+}
+
+// Normalise and round to FP16 into out[row].
+__device__ __forceinline__ void write_output(const LayerArgs &a, int row, int head0, int g, const float (&o)[4][4],
+                                             float l0, float l1) {
+    __half *dst = a.out + row * a.out_stride;
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+        const int d = 16 * mt + g;
+        dst[head0 * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][0], l0));
+        dst[(head0 + 1) * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][1], l1));
+        dst[head0 * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][2], l0));
+        dst[(head0 + 1) * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][3], l1));
+    }
+}
+
+// Three 4-stage CTAs fit an SM's shared memory; the bound holds registers to
+// match (65536 / (3 * 128) = 170 per thread).
 template <int STAGES, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     decode_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ LayerArgs a) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
 
-    const int begin = blockIdx.x * a.blocks_per_cta;
-    const int end = min(begin + a.blocks_per_cta, a.total_blocks);
+    int begin, end;
+    piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, blockIdx.x, begin, end);
     if (begin >= end) return;
 
     const int warp = threadIdx.x >> 5;
@@ -278,13 +403,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int32_t k_rows = (a.layer * 2 + 0) * a.num_blocks * kBlockTokens;
     const int32_t v_rows = (a.layer * 2 + 1) * a.num_blocks * kBlockTokens;
 
-    // Producer state (used by lane 0 only): the next global block to fetch.
+    const uint64_t policy = pkv::l2_policy_evict_first();  // the KV stream is read once
+
+    // Producer state: the next global block to fetch (tracked by every lane;
+    // lane 0 issues).  The physical block ids of the range are held in
+    // registers, 32 at a time (lane j holds the window's j-th id), and the
+    // next window is loaded a whole window ahead, so a refill never waits on
+    // a global load of the block table.
     int next_fetch = begin;
-    if (lane == 0) {
+    int ids = begin + lane < end ? a.flat[begin + lane] : 0;
+    int ids_next = begin + 32 + lane < end ? a.flat[begin + 32 + lane] : 0;
+    {
         const int n = min(STAGES, end - begin);
         for (int s = 0; s < n; ++s) {
-            issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp,
-                        tiles + s * kStageBytes, bar0 + 8 * s, a.error_flag);
+            const int32_t block = __shfl_sync(0xffffffffu, ids, s);
+            if (lane == 0) {
+                issue_block(&pool_map, block, a.num_blocks, k_rows, v_rows, warp, tiles + s * kStageBytes,
+                            bar0 + 8 * s, a.error_flag, policy);
+            }
             ++next_fetch;
         }
     }
@@ -311,24 +447,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         row_first = lo_value;
     }
 
-    RowHead head = row_head(a, row);
-    RowHead head1 = row + 1 < a.batch ? row_head(a, row + 1) : RowHead{0, 0};
-    RowHead head2 = row + 2 < a.batch ? row_head(a, row + 2) : RowHead{0, 0};
+    RowWindow rows = load_row_window(a, row, lane);
+    prefetch_window<FUSED>(a, rows, end, lane, warp);
+    RowHead head = window_head(rows, row);
     RowBody body, body1;
     row_body<FUSED>(a, row, head, warp, lane, body);
 
     int consumed = 0;
-    bool failed = false;
+    bool failed = false;        // a bounded wait ran out
+    bool failed_range = false;  // the range runs past the last row
     int i = begin;
     while (true) {
         const int row_last = head.last;
         const int seg_end = min(end, row_last);
         const int length = head.length;
         const bool has_next = row_last < end;
-        // Prefetch: the next row's body (its head arrived a segment ago) and
-        // the head three rows ahead.
-        if (has_next) row_body<FUSED>(a, row + 1, head1, warp, lane, body1);
-        const RowHead head3 = (has_next && row + 3 < a.batch) ? row_head(a, row + 3) : RowHead{0, 0};
+        // Load the next row's body now; it is used at the next row switch.
+        RowHead head1{0, 0};
+        if (has_next && row + 1 >= a.batch) {
+            // prefix[batch] < end: the caller's prefix and total_blocks disagree.
+            if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
+            failed_range = true;
+        } else if (has_next) {
+            if (row + 1 - rows.base >= 32) {  // past the window (a range of over 32 rows)
+                rows = load_row_window(a, row + 1, lane);
+                prefetch_window<FUSED>(a, rows, end, lane, warp);
+            }
+            head1 = window_head(rows, row + 1);
+            row_body<FUSED>(a, row + 1, head1, warp, lane, body1);
+        }
 
         // Q^T fragments (B operand): lane holds dims 16ks + 2t + {0,1} and
         // 16ks + 8 + 2t + {0,1} of head 8*warp + g.
@@ -430,8 +577,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Hand the stage back to the TMA pipeline before the math.  The
             // refill is issued after every lane holds its fragments (it takes a
-            // value computed from all of them, after a warp barrier) and after a
-            // proxy fence ordering this stage's generic accesses before it.
+            // value computed from all of them, after the warp-wide shuffle that
+            // hands lane 0 the block id) and after a proxy fence ordering this
+            // stage's generic accesses before it.
             {
                 uint32_t ready = 0;
 #pragma unroll
@@ -440,10 +588,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 asm volatile("" ::"r"(ready) : "memory");
                 pkv::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && next_fetch < end) {
-                    issue_block(&pool_map, a.flat[next_fetch], a.num_blocks, k_rows, v_rows, warp, ktile,
-                                bar0 + 8 * stage, a.error_flag, ready);
+                if (next_fetch < end) {
+                    const int slot = (next_fetch - begin) & 31;
+                    if (slot == 0) {
+                        // Entering the next window of block ids; prefetch the one after it.
+                        ids = ids_next;
+                        const int ahead = next_fetch + 32 + lane;
+                        ids_next = ahead < end ? a.flat[ahead] : 0;
+                    }
+                    const int32_t block = __shfl_sync(0xffffffffu, ids, slot);
+                    if (lane == 0) {
+                        issue_block(&pool_map, block, a.num_blocks, k_rows, v_rows, warp, ktile,
+                                    bar0 + 8 * stage, a.error_flag, policy, ready);
+                    }
                     ++next_fetch;
                 }
             }
@@ -494,52 +651,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         l0 = warp_sum8(l0);
         l1 = warp_sum8(l1);
         const int head0 = warp * kGroup + 2 * t;  // heads of o[.][0|2] and o[.][1|3]
-        const int cta_first = row_first / a.blocks_per_cta;
-        const int cta_last = (row_last - 1) / a.blocks_per_cta;
-        if (cta_first == cta_last) {
-            __half *dst = a.out + row * a.out_stride;
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int d = 16 * mt + g;
-                dst[head0 * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][0], l0));
-                dst[(head0 + 1) * kHeadDim + d] = __float2half_rn(__fdiv_rn(o[mt][1], l1));
-                dst[head0 * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][2], l0));
-                dst[(head0 + 1) * kHeadDim + d + 8] = __float2half_rn(__fdiv_rn(o[mt][3], l1));
-            }
-        } else {
-            const int64_t index = static_cast<int64_t>(row) + blockIdx.x;
-            float *po = a.part_o + index * kQueryHeads * kHeadDim;
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const int d = 16 * mt + g;
-                po[head0 * kHeadDim + d] = o[mt][0];
-                po[(head0 + 1) * kHeadDim + d] = o[mt][1];
-                po[head0 * kHeadDim + d + 8] = o[mt][2];
-                po[(head0 + 1) * kHeadDim + d + 8] = o[mt][3];
-            }
-            if (g == 0) {
-                float *pml = a.part_ml + index * kQueryHeads * 2;
-                pml[head0 * 2 + 0] = m0;
-                pml[head0 * 2 + 1] = l0;
-                pml[(head0 + 1) * 2 + 0] = m1;
-                pml[(head0 + 1) * 2 + 1] = l1;
-            }
+        if (row_first >= begin && row_last <= end) {  // the whole row is in this CTA's piece
+            write_output(a, row, head0, g, o, l0, l1);
+        } else {  // merged by decode_combine_kernel
+            store_partial(a, static_cast<int64_t>(row) + blockIdx.x, head0, g, o, m0, l0, m1, l1);
         }
-        if (!has_next) break;
+        if (!has_next || failed_range) break;
         ++row;
         row_first = row_last;
         head = head1;
-        head1 = head2;
-        head2 = head3;
         body = body1;
     }
 
-    if (failed) {
-        if (lane == 0) atomicOr(a.error_flag, PKV_DEVICE_WAIT_TIMEOUT);
-        // Let the copies this warp issued finish before its shared memory is released.
-        for (int c = consumed; c < next_fetch - begin; ++c) {
-            pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
-        }
+    if (failed && lane == 0) atomicOr(a.error_flag, PKV_DEVICE_WAIT_TIMEOUT);
+    // Let the copies this warp issued and did not consume finish before its
+    // shared memory is released (none are left when the range completed).
+    for (int c = consumed; c < next_fetch - begin; ++c) {
+        pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
     }
     // The combine kernel (launched as a programmatic dependent) may start.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -550,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // so its launch and prologue overlap the split kernel's tail.
 __global__ void __launch_bounds__(256) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
-    const int32_t *__restrict__ prefix, int32_t batch, int32_t blocks_per_cta,
+    const int32_t *__restrict__ prefix, int32_t batch, Partition partition,
     __half *__restrict__ out, int64_t out_stride) {
     const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -558,8 +686,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
     const int head = pair % kQueryHeads;
     int cta_first = 0, cta_last = 0;
     if (row < batch) {
-        cta_first = prefix[row] / blocks_per_cta;
-        cta_last = (prefix[row + 1] - 1) / blocks_per_cta;
+        cta_first = piece_of(partition, prefix[row]);
+        cta_last = piece_of(partition, prefix[row + 1] - 1);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
@@ -568,7 +696,10 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
         const int64_t idx = (static_cast<int64_t>(row) + c) * kQueryHeads + head;
         const float2 ml = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
         const float2 v = *reinterpret_cast<const float2 *>(part_o + idx * kHeadDim + 2 * lane);
-        merge_partial(M, L, A0, A1, ml.x, ml.y, v.x, v.y);
+        const MergeWeights w = merge_weights(M, ml.x);
+        L = merge_value(L, ml.y, w);
+        A0 = merge_value(A0, v.x, w);
+        A1 = merge_value(A1, v.y, w);
     }
     *reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + 2 * lane) =
         __floats2half2_rn(__fdiv_rn(A0, L), __fdiv_rn(A1, L));
@@ -720,15 +851,49 @@ void launch_decode(int grid, const CUtensorMap &map, const LayerArgs &args, cuda
     }
 }
 
+// Split partials of (batch + grid) (row, piece) slots.
 int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
     return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
+}
+
+// The pieces of (grid, per_cta, big, tail) are nonempty and cover exactly
+// total_blocks blocks.
+bool partition_matches(int32_t total, int32_t grid, int32_t per_cta, int32_t big, int32_t tail) {
+    if (grid < 1 || per_cta < 1 || big < 1 || big > grid || tail < 1) return false;
+    if (big == grid) {
+        return static_cast<int64_t>(grid) * per_cta >= total && static_cast<int64_t>(grid - 1) * per_cta < total;
+    }
+    const int64_t split = static_cast<int64_t>(big) * per_cta;
+    if (split >= total) return false;
+    return grid - big == (total - split + tail - 1) / tail;
+}
+
+// Share of the blocks in big pieces (percent; 100 = the uniform split) and
+// tail piece size; the environment overrides are for tuning sweeps.
+int configured_big_share() {
+    static int share = [] {
+        const char *env = std::getenv("PKV_DECODE_BIG_SHARE");
+        const int v = env ? std::atoi(env) : 100;
+        return (v >= 50 && v <= 100) ? v : 100;
+    }();
+    return share;
+}
+
+int configured_tail_blocks() {
+    static int tail = [] {
+        const char *env = std::getenv("PKV_DECODE_TAIL_BLOCKS");
+        const int v = env ? std::atoi(env) : 4;
+        return (v >= 1 && v <= 64) ? v : 4;
+    }();
+    return tail;
 }
 
 // Checks shared by both entry points; fills the common part of LayerArgs.
 int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
                   const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
-                  int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
-                  int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag, LayerArgs *args) {
+                  int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
+                  int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
+                  int32_t *error_flag, LayerArgs *args) {
     if (pool == nullptr || query == nullptr || lengths == nullptr || prefix == nullptr ||
         flat == nullptr || out == nullptr || error_flag == nullptr) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: null pointer argument");
@@ -736,9 +901,7 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     if (layer < 0 || layer >= PKV_LAYERS) {
         return pkv::fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
     }
-    if (batch < 1 || total_blocks < batch || grid < 1 || blocks_per_cta < 1 ||
-        static_cast<int64_t>(grid) * blocks_per_cta < total_blocks ||
-        static_cast<int64_t>(grid - 1) * blocks_per_cta >= total_blocks) {
+    if (batch < 1 || total_blocks < batch || !partition_matches(total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks)) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: launch plan does not match the batch");
     }
     if (num_blocks < 1 || static_cast<int64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens > INT32_MAX) {
@@ -764,6 +927,8 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.batch = batch;
     x.total_blocks = total_blocks;
     x.blocks_per_cta = blocks_per_cta;
+    x.big_ctas = big_ctas;
+    x.tail_blocks = tail_blocks;
     x.num_blocks = num_blocks;
     x.layer = layer;
     x.out = static_cast<__half *>(out);
@@ -794,8 +959,9 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStr
     attribute[0].val.programmaticStreamSerializationAllowed = 1;
     config.attrs = attribute;
     config.numAttrs = 1;
+    const Partition partition{args.total_blocks, args.blocks_per_cta, args.big_ctas, args.tail_blocks};
     e = cudaLaunchKernelEx(&config, decode_combine_kernel, static_cast<const float *>(args.part_o),
-                           static_cast<const float *>(args.part_ml), args.prefix, args.batch, args.blocks_per_cta,
+                           static_cast<const float *>(args.part_ml), args.prefix, args.batch, partition,
                            args.out, args.out_stride);
     if (e != cudaSuccess) {
         return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
@@ -806,7 +972,8 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStr
 }  // namespace
 
 extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
-                               int32_t *out_blocks_per_cta, int64_t *out_workspace_bytes) {
+                               int32_t *out_blocks_per_cta, int32_t *out_big_ctas, int32_t *out_tail_blocks,
+                               int64_t *out_workspace_bytes) {
     pkv::clear_error();
     if (batch < 1 || total_blocks < batch) {
         return pkv::fail(PKV_VALUE_ERROR, "decode plan needs batch >= 1 and a nonempty block per row");
@@ -815,10 +982,26 @@ extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_bloc
     int rc = device_info(device, &info);
     if (rc) return rc;
     const int64_t slots = static_cast<int64_t>(info.sms) * info.ctas_per_sm;
-    const int32_t per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
-    const int32_t grid = (total_blocks + per_cta - 1) / per_cta;
+    const int share = configured_big_share();
+    const int tail = configured_tail_blocks();
+    // Big pieces fill every CTA slot once; the rest goes to tail pieces.  A
+    // batch too small for pieces well above the tail size is split evenly.
+    const int64_t big_per_cta = static_cast<int64_t>(total_blocks) * share / (100 * slots);
+    int32_t grid, per_cta, big;
+    if (share < 100 && big_per_cta >= 2 * tail) {
+        per_cta = static_cast<int32_t>(big_per_cta);
+        big = static_cast<int32_t>(slots);
+        const int64_t split = static_cast<int64_t>(big) * per_cta;
+        grid = big + static_cast<int32_t>((total_blocks - split + tail - 1) / tail);
+    } else {
+        per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
+        grid = (total_blocks + per_cta - 1) / per_cta;
+        big = grid;
+    }
     *out_grid = grid;
     *out_blocks_per_cta = per_cta;
+    *out_big_ctas = big;
+    *out_tail_blocks = big == grid ? per_cta : tail;
     *out_workspace_bytes = workspace_bytes_for(batch, grid);
     return PKV_OK;
 }
@@ -827,13 +1010,13 @@ extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_
                                     const void *query, int64_t query_stride, const int32_t *lengths,
                                     const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
                                     int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
-                                    void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
-                                    int32_t *error_flag, void *stream) {
+                                    int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
+                                    void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
     int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
-                           total_blocks, grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes,
-                           error_flag, &args);
+                           total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, workspace,
+                           workspace_bytes, error_flag, &args);
     if (rc) return rc;
     int device = 0;
     cudaGetDevice(&device);
@@ -848,13 +1031,14 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
                                 int64_t query_stride, const void *key, const void *value, int64_t kv_stride,
                                 const void *rope_table, const int32_t *lengths, const int32_t *prefix,
                                 const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                                int32_t grid, int32_t blocks_per_cta, void *out, int64_t out_stride,
-                                void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
+                                int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks,
+                                void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
+                                int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
     int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
-                           total_blocks, grid, blocks_per_cta, out, out_stride, workspace, workspace_bytes,
-                           error_flag, &args);
+                           total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, workspace,
+                           workspace_bytes, error_flag, &args);
     if (rc) return rc;
     if (key == nullptr || value == nullptr || rope_table == nullptr) {
         return pkv::fail(PKV_VALUE_ERROR, "decode layer: key, value and RoPE table are required");
@@ -891,7 +1075,6 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
 namespace {
 
 constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB, held by every device that loads the library
-constexpr int kNoAllocMaxSlots = static_cast<int>(kNoAllocScratchBytes / (kPartialFloats * sizeof(float)));  // 992
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchBytes / sizeof(float)];
@@ -953,14 +1136,16 @@ int noalloc_pool_map(const void *pool, int32_t num_blocks, CUtensorMap *map) {
 extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                             int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
                                             const int32_t *flat, const int32_t *cta_rows, int32_t batch,
-                                            int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, void *out,
-                                            int64_t out_stride, int32_t *error_flag, void *stream) {
+                                            int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                            int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
+                                            int32_t *error_flag, void *stream) {
     pkv::clear_error();
-    if (static_cast<int64_t>(batch) + grid > kNoAllocMaxSlots) {
+    if (batch < 0 || grid < 0 || workspace_bytes_for(batch, grid) > kNoAllocScratchBytes) {
         return pkv::fail(PKV_VALUE_ERROR,
-                         "no-alloc decode attention: batch + grid = " + std::to_string(int64_t(batch) + grid) +
-                             " exceeds the static scratch limit of " + std::to_string(kNoAllocMaxSlots) +
-                             " (8 MiB of split partials); use pkv_decode_attention with a workspace");
+                         "no-alloc decode attention: the plan needs " +
+                             std::to_string(workspace_bytes_for(batch, grid)) +
+                             " bytes of split partials, over the static scratch limit of 8388608 (8 MiB);"
+                             " use pkv_decode_attention with a workspace");
     }
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
@@ -970,8 +1155,8 @@ extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks
     if (rc) return rc;
     LayerArgs args;
     rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
-                       total_blocks, grid, blocks_per_cta, out, out_stride, scratch, kNoAllocScratchBytes,
-                       error_flag, &args);
+                       total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, scratch,
+                       kNoAllocScratchBytes, error_flag, &args);
     if (rc) return rc;
     CUtensorMap map;
     if ((rc = noalloc_pool_map(pool, num_blocks, &map))) return rc;

@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 from torch import Tensor
 
@@ -20,6 +21,12 @@ _LAYERS = 22
 _KV_HEADS = 4
 _QUERY_HEADS = 32
 _HEAD_DIM = 64
+_PARTIAL_BYTES = _QUERY_HEADS * (_HEAD_DIM + 2) * 4  # one split partial: (m, l, O) of 32 heads, FP32
+
+
+def workspace_bytes(batch: int, grid: int) -> int:
+    """Workspace of a plan: one split partial per (row, piece) slot, batch + grid slots."""
+    return (batch + grid) * _PARTIAL_BYTES
 
 
 def _ptr(tensor: Tensor | None) -> ctypes.c_void_p:
@@ -108,22 +115,62 @@ def append_kv(
 
 @dataclass(frozen=True, slots=True)
 class DecodePlan:
+    """Split of a batch's flat block list into one contiguous piece per CTA.
+
+    ``big_ctas`` pieces of ``blocks_per_cta`` blocks come first, then
+    ``grid - big_ctas`` pieces of ``tail_blocks`` blocks; ``big_ctas == 0``
+    stands for the uniform split (every piece ``blocks_per_cta`` blocks).
+    """
+
     grid: int
     blocks_per_cta: int
     workspace_bytes: int
+    big_ctas: int = 0
+    tail_blocks: int = 0
+
+    @classmethod
+    def split(cls, batch: int, total_blocks: int, blocks_per_cta: int, big_ctas: int = 0,
+              tail_blocks: int = 0) -> DecodePlan:
+        """A plan with the given piece sizes (pkv_decode_plan picks its own)."""
+        if big_ctas == 0:
+            grid = -(-total_blocks // blocks_per_cta)
+        else:
+            grid = big_ctas + -(-(total_blocks - big_ctas * blocks_per_cta) // tail_blocks)
+        return cls(grid, blocks_per_cta, workspace_bytes(batch, grid), big_ctas, tail_blocks)
+
+    def pieces(self) -> tuple[int, int]:
+        """(big_ctas, tail_blocks) as the C ABI takes them."""
+        if self.big_ctas == 0:
+            return self.grid, self.blocks_per_cta
+        return self.big_ctas, self.tail_blocks
+
+    def piece_starts(self) -> np.ndarray:
+        """First global block of every piece, int64 [grid]."""
+        big, tail = self.pieces()
+        index = np.arange(self.grid, dtype=np.int64)
+        return np.where(index < big, index * self.blocks_per_cta, big * self.blocks_per_cta + (index - big) * tail)
 
 
 def decode_plan(device: torch.device, batch: int, total_blocks: int) -> DecodePlan:
     grid = ctypes.c_int32()
     per_cta = ctypes.c_int32()
+    big = ctypes.c_int32()
+    tail = ctypes.c_int32()
     workspace = ctypes.c_int64()
     index = device.index if device.index is not None else torch.cuda.current_device()
     check(
         lib.pkv_decode_plan(
-            index, batch, total_blocks, ctypes.byref(grid), ctypes.byref(per_cta), ctypes.byref(workspace)
+            index,
+            batch,
+            total_blocks,
+            ctypes.byref(grid),
+            ctypes.byref(per_cta),
+            ctypes.byref(big),
+            ctypes.byref(tail),
+            ctypes.byref(workspace),
         )
     )
-    return DecodePlan(grid.value, per_cta.value, workspace.value)
+    return DecodePlan(grid.value, per_cta.value, workspace.value, big.value, tail.value)
 
 
 def decode_attention(
@@ -166,6 +213,7 @@ def decode_attention(
             total_blocks,
             plan.grid,
             plan.blocks_per_cta,
+            *plan.pieces(),
             _ptr(out),
             out.stride(0),
             _ptr(workspace),
@@ -230,6 +278,7 @@ def decode_layer(
             total_blocks,
             plan.grid,
             plan.blocks_per_cta,
+            *plan.pieces(),
             _ptr(out),
             out.stride(0),
             _ptr(workspace),

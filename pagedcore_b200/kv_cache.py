@@ -79,7 +79,7 @@ class DecodeBatch:
     lengths: Tensor
     prefix: Tensor
     flat: Tensor
-    cta_rows: Tensor  # [grid][2]: first row of each CTA's block range and its first block
+    cta_rows: Tensor  # [grid][2]: row holding the first block of each CTA's piece, and that row's first block
     total_blocks: int
     plan: kernels.DecodePlan
     host_lengths: np.ndarray
@@ -395,12 +395,14 @@ class KVAllocator:
         fixed = staged.launch_args
         if fixed is None:
             fixed = staged.launch_args = self._decode_layer_args(self.staged_decode_batch(), count)
-        pool_ptr, num_blocks, rope, lengths, prefix, flat, cta_rows, total, grid, per_cta, ws, ws_bytes, err, stream = fixed
+        pool_ptr, num_blocks, rope, lengths, prefix, flat, cta_rows, total, grid, per_cta, big, tail, ws, ws_bytes, err, stream = (
+            fixed
+        )
         check(
             lib.pkv_decode_layer(
                 pool_ptr, num_blocks, layer, query.data_ptr(), query.stride(0), key.data_ptr(), value.data_ptr(),
-                key.stride(0), rope, lengths, prefix, flat, cta_rows, count, total, grid, per_cta, out.data_ptr(),
-                out.stride(0), ws, ws_bytes, err, stream,
+                key.stride(0), rope, lengths, prefix, flat, cta_rows, count, total, grid, per_cta, big, tail,
+                out.data_ptr(), out.stride(0), ws, ws_bytes, err, stream,
             )
         )
         self._ledger.decode_mark(-1, layer)
@@ -413,7 +415,8 @@ class KVAllocator:
         return (
             self._pool.data_ptr(), self._pool.shape[2], self._rope.data_ptr(), batch.lengths.data_ptr(),
             batch.prefix.data_ptr(), batch.flat.data_ptr(), batch.cta_rows.data_ptr(), batch.total_blocks,
-            batch.plan.grid, batch.plan.blocks_per_cta, 0 if workspace is None else workspace.data_ptr(),
+            batch.plan.grid, batch.plan.blocks_per_cta, *batch.plan.pieces(),
+            0 if workspace is None else workspace.data_ptr(),
             0 if workspace is None else workspace.numel() * 4, self._error.data_ptr(), self._stream.cuda_stream,
         )
 
@@ -507,7 +510,7 @@ class KVAllocator:
         used = 2 * count + 1 + total
         plan = kernels.decode_plan(self._pool.device, count, total)
         prefix = host[count : 2 * count + 1]
-        starts = np.arange(plan.grid, dtype=np.int64) * plan.blocks_per_cta
+        starts = plan.piece_starts()
         rows = np.searchsorted(prefix, starts, side="right") - 1
         cta_rows = np.stack((rows, prefix[rows]), axis=1).astype(np.int32).reshape(-1)
         device = self._upload_i32(host[:used], cta_rows)

@@ -255,16 +255,17 @@ def test_ragged_batch_matches_oracle() -> None:
     allocator.check_device_errors()
 
 
-@pytest.mark.parametrize("blocks_per_cta", [1, 2, 3, 5, 8, 64, 1000])
-def test_every_split_plan_gives_the_same_answer(blocks_per_cta: int) -> None:
+# (blocks_per_cta, big_ctas, tail_blocks): uniform splits (big_ctas 0) and
+# two-tier splits, big pieces followed by tail pieces.
+@pytest.mark.parametrize("pieces", [(1, 0, 0), (2, 0, 0), (3, 0, 0), (5, 0, 0), (8, 0, 0), (64, 0, 0), (1000, 0, 0), (20, 10, 3), (7, 30, 1), (100, 2, 5)])
+def test_every_split_plan_gives_the_same_answer(pieces: tuple[int, int, int]) -> None:
     device = cuda_device()
     lengths = [1, 16, 17, 33, 250, 700, 2048, 5, 1200]
     allocator, requests = build_batch(lengths, 33, device)
     query = torch.from_numpy(workloads.normal_f16(workloads.rng(33, 8), (len(lengths), 32, 64))).to(device)
     batch = allocator.decode_batch(requests, layer_index=4)
-    grid = (batch.total_blocks + blocks_per_cta - 1) // blocks_per_cta
-    plan = kernels.DecodePlan(grid, blocks_per_cta, (len(lengths) + grid) * 32 * 66 * 4)
-    workspace = torch.empty(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
+    plan = kernels.DecodePlan.split(len(lengths), batch.total_blocks, *pieces)
+    workspace = torch.zeros(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
     out = torch.empty_like(query)
     kernels.decode_attention(allocator.pool, 4, query, batch.lengths, batch.prefix, batch.flat, batch.total_blocks,
                              plan, out, workspace, allocator._error)

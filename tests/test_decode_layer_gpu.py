@@ -76,8 +76,11 @@ def test_fused_layer_matches_separate_path_bit_for_bit() -> None:
     assert [fused.cached_length(r) for r in requests] == [n + 1 for n in LENGTHS]
 
 
-@pytest.mark.parametrize("blocks_per_cta", [1, 2, 3, 7, 16, 300])
-def test_fused_layer_matches_oracle_under_every_plan(blocks_per_cta: int, rope_golden: np.ndarray) -> None:
+# (blocks_per_cta, big_ctas, tail_blocks): uniform splits (big_ctas 0) and
+# two-tier splits, big pieces followed by tail pieces.
+@pytest.mark.parametrize("pieces", [(1, 0, 0), (2, 0, 0), (3, 0, 0), (7, 0, 0), (16, 0, 0), (300, 0, 0), (20, 10, 3),
+                                    (7, 30, 1), (100, 2, 5)])
+def test_fused_layer_matches_oracle_under_every_plan(pieces: tuple[int, int, int], rope_golden: np.ndarray) -> None:
     device = cuda_device()
     (allocator,), requests = build(LENGTHS, 6, device)
     count = len(LENGTHS)
@@ -87,8 +90,7 @@ def test_fused_layer_matches_oracle_under_every_plan(blocks_per_cta: int, rope_g
     with allocator.append_decode(requests):
         staged = allocator._staged
         batch = allocator._upload_batch(staged.requests, staged.handles, -2)
-        grid = (batch.total_blocks + blocks_per_cta - 1) // blocks_per_cta
-        plan = kernels.DecodePlan(grid, blocks_per_cta, (count + grid) * 32 * 66 * 4)
+        plan = kernels.DecodePlan.split(count, batch.total_blocks, *pieces)
         workspace = torch.empty(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
         for layer in range(22):
             allocator.ledger.decode_check(-1, layer)

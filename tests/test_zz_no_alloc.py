@@ -38,6 +38,7 @@ def _noalloc(allocator: KVAllocator, batch, query: torch.Tensor, layer: int, out
         batch.total_blocks,
         batch.plan.grid,
         batch.plan.blocks_per_cta,
+        *batch.plan.pieces(),
         out.data_ptr(),
         out.stride(0),
         allocator._error.data_ptr(),
@@ -84,10 +85,11 @@ def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row() -> None:
 
 
 def test_noalloc_entry_rejects_batches_beyond_its_fixed_array() -> None:
-    # Refused on the host before any launch: batch + grid must not exceed 992.
+    # Refused on the host before any launch: the plan's partials must fit in 8 MiB
+    # ((batch + grid) * 8448 bytes).
     cuda_device()
     status = _lib.lib.pkv_decode_attention_noalloc(
-        None, 1, 0, None, 0, None, None, None, None, 990, 1000, 10, 100, None, 0, None, None
+        None, 1, 0, None, 0, None, None, None, None, 990, 1000, 10, 100, 10, 100, None, 0, None, None
     )
     assert status == _lib.PKV_VALUE_ERROR
-    assert b"exceeds the static scratch limit of 992" in _lib.lib.pkv_last_error()
+    assert b"over the static scratch limit of 8388608" in _lib.lib.pkv_last_error()
