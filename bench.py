@@ -182,6 +182,28 @@ def _traffic_ratio() -> float | None:
     return None
 
 
+def _bind_host_cores(device: int) -> str:
+    """Run this rank on the host cores NVML reports as closest to its GPU.
+
+    Pinned host buffers allocated afterwards then sit in that NUMA node's
+    memory, so the e2e copies do not cross sockets.  Read-only NVML queries.
+    """
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        handle = ClockSampler(device)._handle(pynvml)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cores = {64 * w + b for w, mask in enumerate(words) for b in range(64) if mask >> b & 1}
+        cores &= set(range(os.cpu_count()))
+        if not cores:
+            return "unbound (NVML reported no cores)"
+        os.sched_setaffinity(0, cores)
+        return f"{len(cores)} cores local to GPU {device}"
+    except Exception as error:  # noqa: BLE001 - binding is an optimisation, never required
+        return f"unbound ({error})"
+
+
 class ClockSampler:
     """SM clock and throttle-reason samples (NVML, read-only) every 2 ms of the timed region."""
 
@@ -273,6 +295,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    affinity = _bind_host_cores(local_rank)
     if world > 1:
         from datetime import timedelta
 
@@ -432,6 +455,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     e2e_end.record(stream)
     barrier()
     e2e_ms = e2e_start.elapsed_time(e2e_end)
+    print(f"rank {rank}: timed {elapsed_ms:.2f} ms, e2e {e2e_ms:.2f} ms, host {affinity}", file=sys.stderr, flush=True)
     allocator.check_device_errors()
 
     times = torch.tensor([elapsed_ms, e2e_ms, layer_ms], dtype=torch.float64, device=device)
@@ -493,6 +517,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             },
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
+            "host_affinity": affinity,
         }
         if world == 1 and not args.no_cpu_baseline:
             from threadpoolctl import threadpool_limits
