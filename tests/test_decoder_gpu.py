@@ -1,0 +1,250 @@
+"""TinyLlama paged prefill and decode over the CUDA KV path, against the reference.
+
+Fixtures (tests/golden/make_decoder_golden.py) hold the reference decoder's
+own outputs on the CPU: a reduced model (2 layers repeated 11 times,
+vocabulary 31, MLP width 32) and BASELINE config 3 (full TinyLlama shape,
+N(0, 0.02) weights, 128-token prompt, 128 greedy tokens).  The weights are
+rebuilt here from the same seeds.  CPU and B200 GEMMs round differently, so
+logits are compared within tolerances written below; greedy argmax must
+agree wherever the reference's top two logits are further apart than that
+tolerance (the config 3 run has exact ties).
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import replace
+
+import numpy as np
+import pytest
+import torch
+
+from pagedcore_b200 import decoder
+from pagedcore_b200.decoder import BatchedDecoder, decode_paged, prefill, prefill_paged
+from pagedcore_b200.engine_types import CapacityCounts, KVReservation, RequestId
+from pagedcore_b200.kv_cache import KVAllocator
+from pagedcore_b200.weights import random_weights
+from tests.conftest import ROOT, cuda_device
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = ROOT / "tests" / "golden"
+SMALL_ROWS = (1, 16, 49)
+LOGIT_TOL = 5e-3  # the reference's decode-vs-dense logits tolerance (NUMERICAL_POLICY), reduced model
+CFG3_TOL = 3e-2   # full 22-layer model, CPU vs B200 GEMM rounding accumulated over the stack
+
+
+def small_prompt(tokens: int) -> torch.Tensor:
+    return (torch.arange(tokens)[None] + tokens) % 31
+
+
+@pytest.fixture(scope="module")
+def small():
+    device = cuda_device()
+    weights = random_weights(5, device, layers=2, vocab=31, intermediate=32)
+    return replace(weights, layers=weights.layers * 11)
+
+
+@pytest.fixture(scope="module")
+def golden_small():
+    return np.load(GOLDEN / "decoder_small.npz")
+
+
+def new_allocator(blocks: int, device: torch.device) -> KVAllocator:
+    pool = torch.full((22, 2, blocks, 16, 4, 64), torch.nan, dtype=torch.float16, device=device)
+    return KVAllocator(pool)
+
+
+def prefilled(weights, lengths, device, extra: int = 4) -> tuple[KVAllocator, tuple[RequestId, ...]]:
+    allocator = new_allocator(sum((n + extra + 15) // 16 for n in lengths) + 2, device)
+    requests = tuple(RequestId(f"row{row}") for row in range(len(lengths)))
+    for request, length in zip(requests, lengths, strict=True):
+        allocator.create(KVReservation(request, (length + extra + 15) // 16))
+        prefill_paged(small_prompt(length).to(device), weights, allocator, request)
+    return allocator, requests
+
+
+def test_prefill_logits_match_the_reference(small, golden_small) -> None:
+    device = cuda_device()
+    for tokens in (1, 15, 16, 17, 49):
+        logits, cache = prefill(small_prompt(tokens).to(device), small)
+        assert logits.shape == (1, tokens, 31) and logits.dtype == torch.float16
+        np.testing.assert_allclose(logits[0].float().cpu().numpy(), golden_small[f"prefill_{tokens}"],
+                                   atol=LOGIT_TOL, rtol=LOGIT_TOL)
+        assert len(cache) == 22 and cache[0][0].shape == (1, 4, tokens, 64)
+
+
+def test_prefill_paged_publishes_the_rotated_prompt_into_the_pool(small) -> None:
+    device = cuda_device()
+    allocator = new_allocator(8, device)
+    request = RequestId("prompt")
+    allocator.create(KVReservation(request, 4))
+    ids = small_prompt(49).to(device)
+    expected_logits, cache = prefill(ids, small)
+    logits = prefill_paged(ids, small, allocator, request)
+    torch.testing.assert_close(logits, expected_logits, atol=0, rtol=0)
+    assert allocator.cached_length(request) == 49
+    table = allocator.block_table(request)
+    for layer in (0, 21):
+        key, value = cache[layer]
+        for logical, physical in enumerate(table):
+            start, end = 16 * logical, min(16 * logical + 16, 49)
+            got_k = allocator.pool[layer, 0, physical, : end - start]
+            got_v = allocator.pool[layer, 1, physical, : end - start]
+            torch.testing.assert_close(got_k, key[0, :, start:end].transpose(0, 1), atol=0, rtol=0)
+            torch.testing.assert_close(got_v, value[0, :, start:end].transpose(0, 1), atol=0, rtol=0)
+    with pytest.raises(ValueError, match="empty request cache"):
+        prefill_paged(ids, small, allocator, request)
+
+
+def test_decode_paged_matches_the_reference_over_three_steps(small, golden_small) -> None:
+    device = cuda_device()
+    allocator, requests = prefilled(small, SMALL_ROWS, device)
+    for step in range(3):
+        order = tuple(int(x) for x in golden_small[f"decode_{step}_order"])
+        tokens = torch.tensor([[3 + row + step] for row in order], device=device)
+        logits = decode_paged(tokens, small, allocator, tuple(requests[r] for r in order))
+        assert logits.shape == (3, 1, 31) and logits.dtype == torch.float16
+        np.testing.assert_allclose(logits[:, 0].float().cpu().numpy(), golden_small[f"decode_{step}"],
+                                   atol=LOGIT_TOL, rtol=LOGIT_TOL)
+    assert [allocator.cached_length(r) for r in requests] == [n + 3 for n in SMALL_ROWS]
+    allocator.check_device_errors()
+
+
+def test_decode_paged_rows_do_not_depend_on_the_rest_of_the_batch(small) -> None:
+    # decoder.py's batch-independence property (tests/unit/test_decoder.py:198-239), bit for bit.
+    device = cuda_device()
+    separate, requests = prefilled(small, SMALL_ROWS, device)
+    batched, _ = prefilled(small, SMALL_ROWS, device)
+    for step in range(3):
+        order = requests if step % 2 == 0 else requests[::-1]
+        tokens = torch.tensor([[3 + int(r.removeprefix("row")) + step] for r in order], device=device)
+        expected = torch.cat([decode_paged(tokens[i : i + 1], small, separate, (r,)) for i, r in enumerate(order)])
+        actual = decode_paged(tokens, small, batched, order)
+        torch.testing.assert_close(actual, expected, atol=0, rtol=0)
+    for request in requests:
+        for block in range(len(batched.block_table(request))):
+            for a, b in zip(batched.read_block(request, block), separate.read_block(request, block), strict=True):
+                torch.testing.assert_close(a, b, atol=0, rtol=0)
+
+
+def test_batched_decoder_matches_decode_paged(small) -> None:
+    device = cuda_device()
+    per_row, requests = prefilled(small, SMALL_ROWS, device)
+    fused, _ = prefilled(small, SMALL_ROWS, device)
+    engine = BatchedDecoder(small)
+    for step in range(3):
+        tokens = torch.tensor([[5 + row + step] for row in range(3)], device=device)
+        expected = decode_paged(tokens, small, per_row, requests)
+        actual = engine.step(tokens, fused, requests)
+        torch.testing.assert_close(actual, expected, atol=LOGIT_TOL, rtol=LOGIT_TOL)
+        assert torch.equal(actual.argmax(-1), expected.argmax(-1))
+    assert fused.capacity() == per_row.capacity()
+    for request in requests:
+        assert fused.cached_length(request) == per_row.cached_length(request)
+        for block in range(len(fused.block_table(request))):
+            for a, b in zip(fused.read_block(request, block), per_row.read_block(request, block), strict=True):
+                torch.testing.assert_close(a, b, atol=2e-3, rtol=2e-3)
+    fused.check_device_errors()
+
+
+@pytest.mark.parametrize("fault", ["attention", "logits"])
+def test_a_failed_decode_leaves_every_row_unchanged_and_can_be_retried(small, fault, monkeypatch) -> None:
+    device = cuda_device()
+    allocator, requests = prefilled(small, (15, 16), device, extra=2)
+    tables = [allocator.block_table(r) for r in requests]
+    counts = allocator.capacity()
+    tokens = torch.tensor([[3], [7]], device=device)
+    name = "paged_attention" if fault == "attention" else "final_logits"
+    original = getattr(decoder, name)
+    calls = 0
+
+    def fail(*args, **kwargs):
+        nonlocal calls
+        calls += 1
+        if calls == (3 if fault == "attention" else 1):
+            raise RuntimeError("injected decode failure")
+        return original(*args, **kwargs)
+
+    with monkeypatch.context() as patch:
+        patch.setattr(decoder, name, fail)
+        with pytest.raises(RuntimeError, match="injected decode failure"):
+            decode_paged(tokens, small, allocator, requests)
+    assert allocator.capacity() == counts
+    assert [allocator.block_table(r) for r in requests] == tables
+    assert [allocator.cached_length(r) for r in requests] == [15, 16]
+    fresh, _ = prefilled(small, (15, 16), device, extra=2)
+    torch.testing.assert_close(decode_paged(tokens, small, allocator, requests),
+                               decode_paged(tokens, small, fresh, requests), atol=0, rtol=0)
+
+
+def test_decode_rejects_bad_batches_without_touching_the_cache(small) -> None:
+    device = cuda_device()
+    allocator, requests = prefilled(small, (15, 16), device, extra=2)
+    counts = allocator.capacity()
+    tokens = torch.tensor([[3], [7]], device=device)
+    with pytest.raises(ValueError, match="int64"):
+        decode_paged(tokens.float(), small, allocator, requests)
+    with pytest.raises(ValueError, match="same device"):
+        decode_paged(tokens.cpu(), small, allocator, requests)
+    with pytest.raises(ValueError, match="22 decoder layers"):
+        decode_paged(tokens, replace(small, layers=small.layers[:2]), allocator, requests)
+    with pytest.raises(KeyError):
+        decode_paged(tokens, small, allocator, (requests[0], RequestId("unknown")))
+    assert allocator.capacity() == counts
+
+
+# -- BASELINE config 3 ----------------------------------------------------------
+@pytest.fixture(scope="module")
+def cfg3():
+    record = json.loads((GOLDEN / "decoder_cfg3.json").read_text())
+    return record, random_weights(record["seed"], cuda_device())
+
+
+def _teacher_forced(record, step_fn) -> tuple[float, int, list[int]]:
+    """Run the reference's token sequence through `step_fn`; compare every step.
+
+    Returns (max |logit - reference| over the top-8 ids of every step, steps
+    whose argmax agrees, steps where it disagrees).
+    """
+    worst, agree, disagree = 0.0, 0, []
+    for step, expected in enumerate(record["steps"]):
+        logits = step_fn(step).float().cpu()
+        ids = torch.tensor(expected["top_ids"])
+        worst = max(worst, float((logits[ids] - torch.tensor(expected["top_logits"])).abs().max()))
+        gap = expected["top_logits"][0] - expected["top_logits"][1]
+        if int(logits.argmax()) == expected["top_ids"][0]:
+            agree += 1
+        elif gap > 2 * CFG3_TOL:
+            disagree.append(step)
+    return worst, agree, disagree
+
+
+@pytest.mark.parametrize("path", ["per_row", "batched"])
+def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
+    record, weights = cfg3
+    device = cuda_device()
+    allocator = new_allocator(20, device)
+    request = RequestId("cfg3")
+    allocator.create(KVReservation(request, 16))
+    prompt = torch.tensor([record["prompt"]], dtype=torch.int64, device=device)
+    prompt_logits = prefill_paged(prompt, weights, allocator, request)[0, -1]
+    engine = BatchedDecoder(weights)
+    ids = record["greedy_ids"]
+
+    def step_fn(step: int) -> torch.Tensor:
+        if step == 0:
+            return prompt_logits
+        token = torch.tensor([[ids[step - 1]]], dtype=torch.int64, device=device)
+        if path == "per_row":
+            return decode_paged(token, weights, allocator, (request,))[0, 0]
+        return engine.step(token, allocator, (request,))[0, 0]
+
+    worst, agree, disagree = _teacher_forced(record, step_fn)
+    assert worst < CFG3_TOL, worst
+    assert disagree == []  # argmax differs only where the reference's top two are within 2 * tolerance
+    assert agree >= 120
+    assert allocator.cached_length(request) == 128 + 127
+    allocator.check_device_errors()
+    allocator.release_all(request)
+    assert allocator.capacity() == CapacityCounts(20, 20, 0, 0, 0, 0)
