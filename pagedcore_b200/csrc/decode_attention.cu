@@ -378,6 +378,10 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
 
+    // The kernel is launched as a programmatic dependent of whatever precedes
+    // it on the stream, so its launch overlaps that kernel's tail; nothing here
+    // touches memory before that kernel has completed and its writes are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     int begin, end;
     piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, blockIdx.x, begin, end);
     if (begin >= end) return;
@@ -785,6 +789,9 @@ template <int STAGES, bool FUSED>
 int prepare_kernel(int *ctas_per_sm) {
     auto kernel = decode_kernel<STAGES, FUSED>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<STAGES>());
+    if (e == cudaSuccess) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    }
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, kThreads, smem_bytes<STAGES>());
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("occupancy query: ") + cudaGetErrorString(e));
@@ -828,6 +835,14 @@ int device_info(int device, DeviceInfo *info) {
         case 8: rc = prepare_both<8>(&d.ctas_per_sm); break;
         default: rc = prepare_both<6>(&d.ctas_per_sm); break;
     }
+    if (rc == PKV_OK) {
+        // The combine needs no shared memory, but an SM that alternates between
+        // it and the split kernel would otherwise re-partition L1 and shared
+        // memory at every layer; keeping the split kernel's partition avoids that.
+        const cudaError_t e = cudaFuncSetAttribute(decode_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                                   cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) rc = pkv::fail(PKV_CUDA_ERROR, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    }
     cudaSetDevice(previous);
     if (rc) return rc;
     if (d.ctas_per_sm < 1) d.ctas_per_sm = 1;
@@ -837,17 +852,28 @@ int device_info(int device, DeviceInfo *info) {
 }
 
 template <bool FUSED>
-void launch_decode(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream) {
+cudaError_t launch_decode(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream) {
+    // Programmatic dependent launch: see the griddepcontrol.wait at the top of
+    // decode_kernel.
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(kThreads);
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
     switch (configured_stages()) {
         case 4:
-            decode_kernel<4, FUSED><<<grid, kThreads, smem_bytes<4>(), stream>>>(map, args);
-            break;
+            config.dynamicSmemBytes = smem_bytes<4>();
+            return cudaLaunchKernelEx(&config, decode_kernel<4, FUSED>, map, args);
         case 8:
-            decode_kernel<8, FUSED><<<grid, kThreads, smem_bytes<8>(), stream>>>(map, args);
-            break;
+            config.dynamicSmemBytes = smem_bytes<8>();
+            return cudaLaunchKernelEx(&config, decode_kernel<8, FUSED>, map, args);
         default:
-            decode_kernel<6, FUSED><<<grid, kThreads, smem_bytes<6>(), stream>>>(map, args);
-            break;
+            config.dynamicSmemBytes = smem_bytes<6>();
+            return cudaLaunchKernelEx(&config, decode_kernel<6, FUSED>, map, args);
     }
 }
 
@@ -943,8 +969,7 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
 // as its programmatic dependent on the same stream.
 template <bool FUSED>
 int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream, const char *what) {
-    launch_decode<FUSED>(grid, map, args, stream);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_decode<FUSED>(grid, map, args, stream);
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string(what) + " launch failed: " + cudaGetErrorString(e));
     if (grid == 1) return PKV_OK;
     const int warps_per_cta = 8;

@@ -1,19 +1,27 @@
 """Boundary value types of the paged KV path.
 
 Same names, fields and validation as PagedCore's engine_types
-(src/pagedcore/engine_types.py:7-11, 170-219), so values built by a caller of
-the reference are accepted unchanged.  The request-lifecycle types of that
-module belong to the service layer and are not part of this path.
+(src/pagedcore/engine_types.py:7-11, 63-65, 170-219), so values built by a
+caller of the reference are accepted unchanged.  The other request-lifecycle
+types of that module belong to the service layer and are not part of this path.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
+from enum import StrEnum
 from typing import NewType, TypeAlias
 
 RequestId = NewType("RequestId", str)
 BlockId = NewType("BlockId", int)
 BlockTable: TypeAlias = tuple[BlockId, ...]
+
+
+class FinishReason(StrEnum):
+    """Why a generation stopped (engine_types.py:63-65)."""
+
+    EOS = "eos"
+    LENGTH = "length"
 
 
 @dataclass(frozen=True, slots=True)
