@@ -99,6 +99,73 @@ class _Staged:
     launch_args: tuple | None = None  # fixed pkv_decode_layer arguments of this step
 
 
+@dataclass(slots=True)
+class _UploadSlot:
+    host: Tensor  # pinned int32
+    device: Tensor  # int32 on the pool device
+    copied: torch.cuda.Event  # the host -> device copy into ``device`` has finished
+    released: torch.cuda.Event  # the last kernel reading ``device`` has finished
+    used: bool = False
+
+
+class _StepUploads:
+    """Per-step int32 tables, copied to the device on a side stream.
+
+    Two slots alternate: the tables of step i+1 are written and copied while
+    step i's kernels still read the other slot, so the copy is done when the
+    compute stream reaches step i+1 and its wait costs nothing.  A slot is
+    reused only after the compute stream has passed the step that read it.
+    """
+
+    def __init__(self, device: torch.device, compute: torch.cuda.Stream) -> None:
+        self._device = device
+        self._compute = compute
+        self._copy = torch.cuda.Stream(device)
+        self._slots: list[_UploadSlot] = []
+        self._next = 0
+
+    def _ensure(self, count: int) -> None:
+        if self._slots and self._slots[0].host.numel() >= count:
+            return
+        # Growing: no copy or kernel may still use the old buffers.
+        torch.cuda.synchronize(self._device)
+        size = max(count, 2 * self._slots[0].host.numel() if self._slots else 8192)
+        self._slots = [
+            _UploadSlot(
+                torch.empty(size, dtype=torch.int32, pin_memory=True),
+                torch.empty(size, dtype=torch.int32, device=self._device),
+                torch.cuda.Event(),
+                torch.cuda.Event(),
+            )
+            for _ in range(2)
+        ]
+        self._next = 0
+
+    def upload(self, arrays: Sequence[np.ndarray]) -> tuple[Tensor, _UploadSlot]:
+        count = sum(len(a) for a in arrays)
+        self._ensure(count)
+        slot = self._slots[self._next]
+        self._next ^= 1
+        if slot.used:
+            slot.copied.synchronize()  # its pinned buffer is no longer being read
+            self._copy.wait_event(slot.released)  # nor its device buffer
+        view = slot.host.numpy()
+        offset = 0
+        for array in arrays:
+            view[offset : offset + len(array)] = array
+            offset += len(array)
+        with torch.cuda.stream(self._copy):
+            slot.device[:count].copy_(slot.host[:count], non_blocking=True)
+        slot.copied.record(self._copy)
+        self._compute.wait_event(slot.copied)
+        slot.used = True
+        return slot.device[:count], slot
+
+    def release(self, slot: _UploadSlot) -> None:
+        """Every kernel reading the slot has been enqueued on the compute stream."""
+        slot.released.record(self._compute)
+
+
 class KVAllocator:
     """Assign blocks within an existing CUDA pool (kv_cache.py:63-90).
 
@@ -130,6 +197,7 @@ class KVAllocator:
         self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
         self._rope = device_table(pool.device)
         self._workspace: Tensor | None = None
+        self._uploads = _StepUploads(pool.device, self._stream)
 
     # -- plumbing -------------------------------------------------------------
     @property
@@ -266,15 +334,23 @@ class KVAllocator:
         except KeyError as error:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
-        meta = self._upload_i32(slots, positions)
         count = len(request_ids)
+        try:
+            # The staged view (every row with its new token) is what the fused
+            # decode layer reads; its tables travel with the slots in one copy.
+            host, total, plan, cta_rows = self._batch_tables(request_ids, handles, _VIEW_STAGED)
+            device, upload = self._uploads.upload((slots, positions, host, cta_rows))
+        except BaseException:
+            self._ledger.decode_abort()
+            raise
         self._staged = _Staged(
             requests=request_ids,
             handles=handles,
             rows={request_id: row for row, request_id in enumerate(request_ids)},
-            slots=meta[:count],
-            positions=meta[count:],
+            slots=device[:count],
+            positions=device[count : 2 * count],
             host_positions=positions,
+            staged_batch=self._device_batch(request_ids, host, total, plan, device[2 * count :]),
         )
         try:
             yield
@@ -285,6 +361,7 @@ class KVAllocator:
             self._ledger.decode_commit()
         finally:
             self._staged = None
+            self._uploads.release(upload)
 
     @torch.inference_mode()
     def write_decode_layer(self, request_id: RequestId, layer_index: int, key: Tensor, value: Tensor) -> None:
@@ -421,7 +498,10 @@ class KVAllocator:
         )
 
     def staged_decode_batch(self) -> DecodeBatch:
-        """Device tables of the staged batch with every row's new token included."""
+        """Device tables of the staged batch with every row's new token included.
+
+        Valid until the staged step ends (its buffer is reused two steps later).
+        """
         staged = self._staged
         if staged is None:
             raise RuntimeError("decode writes require a staged append")
@@ -497,7 +577,10 @@ class KVAllocator:
             staged.batch = batch
         return batch
 
-    def _upload_batch(self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int) -> DecodeBatch:
+    def _batch_tables(
+        self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int
+    ) -> tuple[np.ndarray, int, kernels.DecodePlan, np.ndarray]:
+        """Host tables of a batch at ``layer``: [lengths | prefix | flat], blocks, plan, cta_rows."""
         count = len(request_ids)
         if count == 0:
             raise ValueError("attention requires a nonempty batch")
@@ -507,13 +590,18 @@ class KVAllocator:
         except KeyError as error:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
-        used = 2 * count + 1 + total
         plan = kernels.decode_plan(self._pool.device, count, total)
         prefix = host[count : 2 * count + 1]
-        starts = plan.piece_starts()
-        rows = np.searchsorted(prefix, starts, side="right") - 1
+        rows = np.searchsorted(prefix, plan.piece_starts(), side="right") - 1
         cta_rows = np.stack((rows, prefix[rows]), axis=1).astype(np.int32).reshape(-1)
-        device = self._upload_i32(host[:used], cta_rows)
+        return host[: 2 * count + 1 + total], total, plan, cta_rows
+
+    @staticmethod
+    def _device_batch(
+        request_ids: tuple[RequestId, ...], host: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor
+    ) -> DecodeBatch:
+        """A DecodeBatch over ``device`` = [lengths | prefix | flat | cta_rows] as uploaded."""
+        count, used = len(request_ids), len(host)
         return DecodeBatch(
             requests=request_ids,
             lengths=device[:count],
@@ -524,6 +612,10 @@ class KVAllocator:
             plan=plan,
             host_lengths=host[:count].copy(),
         )
+
+    def _upload_batch(self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int) -> DecodeBatch:
+        host, total, plan, cta_rows = self._batch_tables(request_ids, handles, layer)
+        return self._device_batch(request_ids, host, total, plan, self._upload_i32(host, cta_rows))
 
     def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
         """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""
