@@ -37,6 +37,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "paged decode-attn HBM GB/s (% of peak) and decode tokens/s at 1/2/4/8 B200"
 SEQUENCES = 256  # per GPU (config 4); --sequences overrides it for small profiling cases
 LAYERS = 22
+CALIBRATION_STEPS = 8  # staged steps in which KVAllocator(balance="measured") learns its piece weights
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -158,6 +159,8 @@ def _config(n_gpus: int) -> dict:
         "heads": "32 query / 4 KV, head_dim 64, block 16",
         "l2": "inputs larger than L2: each attention launch streams ~0.25 GB of K/V (L2 is 126 MB)",
         "parallelism": f"dp{n_gpus} (independent sequences, one KV pool per GPU, no collective)",
+        "pieces": "one per CTA slot, cut to balance blocks + row switches, weighted by each slot's measured speed "
+                  f"(KVAllocator balance='measured', learnt in {CALIBRATION_STEPS} untimed setup steps, then frozen)",
     }
 
 
@@ -309,11 +312,11 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     total_steps = args.warmup + args.steps
     seed = 4 + 1000 * rank
     # Room for every append of the run: warm-up, plan, timed, e2e warm-up and e2e steps.
-    room = 2 * total_steps + 4
+    room = 2 * total_steps + 4 + CALIBRATION_STEPS
     case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=room)
     context_high = 2048 - room
     pool = torch.empty((22, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
-    allocator = KVAllocator(pool, validation="incremental")
+    allocator = KVAllocator(pool, validation="incremental", balance="measured")
 
     # Fragment the free list with seeded churn, then prefill the batch.
     generator = torch.Generator(device=device).manual_seed(seed)
@@ -355,6 +358,10 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(device)
 
+    # Setup, untimed: the allocator learns each CTA slot's speed over its first
+    # staged steps and then freezes the piece weights.
+    for i in range(CALIBRATION_STEPS):
+        step(*device_inputs[i % 2])
     for i in range(args.warmup):
         step(*device_inputs[i % 2])
     allocator.check_device_errors()

@@ -187,6 +187,18 @@ int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t
                     int32_t *out_blocks_per_cta, int32_t *out_big_ctas, int32_t *out_tail_blocks,
                     int64_t *out_workspace_bytes);
 
+/* Piece tables of a batch (host memory in and out; no device work).  Cuts the
+ * flat list of prefix[batch] blocks into `grid` contiguous, nonempty pieces
+ * (1 <= grid <= prefix[batch]) so that every piece carries the same cost,
+ * where a block costs 1 and each row start inside a piece costs `row_cost`
+ * more (the row switch of the decode kernel), times the piece's relative
+ * speed weights[g] when `weights` (host float [grid], positive) is given.
+ * Writes pieces [grid][4] = (begin, end, first row, that row's first block)
+ * and row_pieces [batch][2] = (first, last piece) of each row.  The result
+ * depends only on the arguments. */
+int pkv_decode_tables(const int32_t *prefix, int32_t batch, int32_t grid, const float *weights, float row_cost,
+                      int32_t *pieces, int32_t *row_pieces);
+
 /* Batched one-token block-table decode attention with GQA (8 query heads per
  * KV head).  Replaces paged_attention (attention.py:14-53) for a whole batch:
  *   out[b,h] = sum_t softmax_t(q[b,h] . K[t, h/8] * 0.125) V[t, h/8]
@@ -197,16 +209,18 @@ int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t
  * int32 device arrays as written by pkv_ledger_batch.  grid / blocks_per_cta /
  * big_ctas / tail_blocks / workspace come from pkv_decode_plan for the same
  * (batch, total_blocks), or describe another partition that covers the
- * blocks exactly.  cta_rows (nullable): int32 [grid][2], for CTA g the row
- * containing the first block of its piece and that row's first block
- * prefix[row]; without it every CTA searches prefix.  Two launches: the split kernel and, when
+ * blocks exactly.  pieces / row_pieces (nullable, both or neither; device):
+ * the tables pkv_decode_tables makes for `grid` pieces, 16- and 4-byte
+ * aligned; with them the pieces are the tables' (grid must match them, the
+ * partition arguments are ignored), without them every CTA takes the
+ * partition's piece and searches prefix for its first row.  Two launches: the split kernel and, when
  * grid > 1, the combine kernel as its programmatic dependent. */
 int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                          int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
-                         const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                         int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks, void *out,
-                         int64_t out_stride, void *workspace, int64_t workspace_bytes, int32_t *error_flag,
-                         void *stream);
+                         const int32_t *flat, const int32_t *pieces, const int32_t *row_pieces, int32_t batch,
+                         int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
+                         int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
+                         int32_t *error_flag, void *stream);
 
 /* One decode layer for a staged batch: the fused form of write_decode_layer
  * (kv_cache.py:221-246) + apply_rope on Q and K (dense.py:33-61) +
@@ -216,15 +230,15 @@ int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, co
  * `layer`, Q is rotated at the same position, and the attention over all
  * lengths[b] tokens is written to out.  query: unrotated FP16 [batch][32][64]
  * (rows query_stride apart); key/value: FP16 [batch][4][64] (rows kv_stride
- * apart); rope_table as for pkv_append_kv.  Plan, workspace and cta_rows as
+ * apart); rope_table as for pkv_append_kv.  Plan, workspace and piece tables as
  * for pkv_decode_attention; one split launch plus, when grid > 1, the
  * combine launch. */
 int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
                      const void *key, const void *value, int64_t kv_stride, const void *rope_table,
-                     const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
-                     int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
-                     int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
-                     int32_t *error_flag, void *stream);
+                     const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *pieces,
+                     const int32_t *row_pieces, int32_t batch, int32_t total_blocks, int32_t grid,
+                     int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
+                     void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream);
 
 /* pkv_decode_attention without any allocation.  No counterpart in the
  * reference: it is for callers that cannot allocate device memory for this
@@ -243,9 +257,10 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
  * and must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
 int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                  int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
-                                 const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                                 int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks,
-                                 void *out, int64_t out_stride, int32_t *error_flag, void *stream);
+                                 const int32_t *flat, const int32_t *pieces, const int32_t *row_pieces, int32_t batch,
+                                 int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
+                                 int32_t tail_blocks, void *out, int64_t out_stride, int32_t *error_flag,
+                                 void *stream);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ],
     ),
     "pkv_decode_plan": (c_int, [c_int32, c_int32, c_int32, i32p, i32p, i32p, i32p, i64p]),
+    "pkv_decode_tables": (c_int, [c_void_p, c_int32, c_int32, c_void_p, ctypes.c_float, c_void_p, c_void_p]),
     "pkv_decode_layer": (
         c_int,
         [
@@ -102,7 +103,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # lengths
             c_void_p,  # prefix
             c_void_p,  # flat
-            c_void_p,  # cta_rows
+            c_void_p,  # pieces
+            c_void_p,  # row_pieces
             c_int32,  # batch
             c_int32,  # total_blocks
             c_int32,  # grid
@@ -128,7 +130,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # lengths
             c_void_p,  # prefix
             c_void_p,  # flat
-            c_void_p,  # cta_rows
+            c_void_p,  # pieces
+            c_void_p,  # row_pieces
             c_int32,  # batch
             c_int32,  # total_blocks
             c_int32,  # grid
@@ -152,7 +155,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # lengths
             c_void_p,  # prefix
             c_void_p,  # flat
-            c_void_p,  # cta_rows
+            c_void_p,  # pieces
+            c_void_p,  # row_pieces
             c_int32,  # batch
             c_int32,  # total_blocks
             c_int32,  # grid

@@ -57,6 +57,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <mutex>
 #include <string>
@@ -113,15 +114,16 @@ struct LayerArgs {
     int64_t out_stride;
     float *part_o;             // [(B + grid)][32][64]
     float *part_ml;            // [(B + grid)][32][2]
-    const int32_t *cta_rows;   // [grid][2]: first row of each CTA's range and its first block (or null)
+    unsigned *cta_ns;          // [grid][4]: each warp's wall time, accumulated over launches (or null)
+    const int32_t *pieces;     // [grid][4]: begin, end, first row and that row's first block of each
+                               // CTA's piece (or null: the Partition below, rows found by search)
     int32_t *error_flag;
 };
 
 // The plan's partition of the flat block list into one contiguous piece per
-// CTA: `big` pieces of `per_cta` blocks, then pieces of `tail` blocks.  The
-// tail pieces are later CTAs of the grid; the hardware starts each on
-// whichever SM frees a slot first, so SMs that stream faster take more of
-// them and all SMs finish together.  big == grid is the uniform partition.
+// CTA when no piece tables are given: `big` pieces of `per_cta` blocks, then
+// pieces of `tail` blocks (big == grid: all pieces per_cta).  pkv_decode_plan
+// makes r pieces of q + 1 blocks and grid - r of q, one per CTA slot.
 struct Partition {
     int32_t total;
     int32_t per_cta;
@@ -382,8 +384,21 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     // it on the stream, so its launch overlaps that kernel's tail; nothing here
     // touches memory before that kernel has completed and its writes are visible.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    int begin, end;
-    piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, blockIdx.x, begin, end);
+    const uint64_t started = pkv::global_timer_ns();
+    int begin, end, row = 0, row_first = 0;
+    if (a.pieces != nullptr) {
+        const int4 piece = reinterpret_cast<const int4 *>(a.pieces)[blockIdx.x];
+        begin = piece.x;
+        end = piece.y;
+        row = piece.z;
+        row_first = piece.w;
+        if (begin < 0 || end > a.total_blocks || row < 0 || row >= a.batch || row_first > begin) {
+            if (threadIdx.x == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
+            return;
+        }
+    } else {
+        piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, blockIdx.x, begin, end);
+    }
     if (begin >= end) return;
 
     const int warp = threadIdx.x >> 5;
@@ -430,12 +445,8 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     }
 
     // First row of the range (the largest b with prefix[b] <= begin) and its
-    // first block: from the host's per-CTA table, else a 32-way search.
-    int row = 0, row_first = 0;
-    if (a.cta_rows != nullptr) {
-        row = a.cta_rows[2 * blockIdx.x];
-        row_first = a.cta_rows[2 * blockIdx.x + 1];
-    } else {
+    // first block: from the piece table, else a 32-way search.
+    if (a.pieces == nullptr) {
         int lo = 0, hi = a.batch - 1, lo_value = 0;
         while (hi > lo) {
             const int step = (hi - lo + 32) / 32;
@@ -673,6 +684,10 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     for (int c = consumed; c < next_fetch - begin; ++c) {
         pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
     }
+    // The host may weight the pieces by each CTA slot's measured speed.
+    if (lane == 0 && a.cta_ns != nullptr) {
+        atomicAdd(&a.cta_ns[4 * blockIdx.x + warp], static_cast<unsigned>(pkv::global_timer_ns() - started));
+    }
     // The combine kernel (launched as a programmatic dependent) may start.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -682,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
 // so its launch and prologue overlap the split kernel's tail.
 __global__ void __launch_bounds__(256) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
-    const int32_t *__restrict__ prefix, int32_t batch, Partition partition,
+    const int32_t *__restrict__ prefix, const int32_t *__restrict__ row_pieces, int32_t batch, Partition partition,
     __half *__restrict__ out, int64_t out_stride) {
     const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -690,8 +705,13 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
     const int head = pair % kQueryHeads;
     int cta_first = 0, cta_last = 0;
     if (row < batch) {
-        cta_first = piece_of(partition, prefix[row]);
-        cta_last = piece_of(partition, prefix[row + 1] - 1);
+        if (row_pieces != nullptr) {
+            cta_first = row_pieces[2 * row];
+            cta_last = row_pieces[2 * row + 1];
+        } else {
+            cta_first = piece_of(partition, prefix[row]);
+            cta_last = piece_of(partition, prefix[row + 1] - 1);
+        }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
@@ -877,9 +897,11 @@ cudaError_t launch_decode(int grid, const CUtensorMap &map, const LayerArgs &arg
     }
 }
 
-// Split partials of (batch + grid) (row, piece) slots.
+// Split partials of (batch + grid) (row, piece) slots, then each CTA's four
+// warp wall-time counters.
 int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
-    return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
+    return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float)) +
+           static_cast<int64_t>(grid) * 4 * static_cast<int64_t>(sizeof(unsigned));
 }
 
 // The pieces of (grid, per_cta, big, tail) are nonempty and cover exactly
@@ -894,29 +916,10 @@ bool partition_matches(int32_t total, int32_t grid, int32_t per_cta, int32_t big
     return grid - big == (total - split + tail - 1) / tail;
 }
 
-// Share of the blocks in big pieces (percent; 100 = the uniform split) and
-// tail piece size; the environment overrides are for tuning sweeps.
-int configured_big_share() {
-    static int share = [] {
-        const char *env = std::getenv("PKV_DECODE_BIG_SHARE");
-        const int v = env ? std::atoi(env) : 100;
-        return (v >= 50 && v <= 100) ? v : 100;
-    }();
-    return share;
-}
-
-int configured_tail_blocks() {
-    static int tail = [] {
-        const char *env = std::getenv("PKV_DECODE_TAIL_BLOCKS");
-        const int v = env ? std::atoi(env) : 4;
-        return (v >= 1 && v <= 64) ? v : 4;
-    }();
-    return tail;
-}
-
 // Checks shared by both entry points; fills the common part of LayerArgs.
 int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const void *query, int64_t query_stride,
-                  const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
+                  const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *pieces,
+                  const int32_t *row_pieces,
                   int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
                   int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
                   int32_t *error_flag, LayerArgs *args) {
@@ -927,15 +930,23 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     if (layer < 0 || layer >= PKV_LAYERS) {
         return pkv::fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
     }
-    if (batch < 1 || total_blocks < batch || !partition_matches(total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks)) {
+    // With piece tables the tables define the pieces; otherwise the partition does.
+    const bool plan_ok = pieces != nullptr
+                             ? grid >= 1 && grid <= total_blocks
+                             : partition_matches(total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks);
+    if (batch < 1 || total_blocks < batch || !plan_ok) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: launch plan does not match the batch");
     }
     if (num_blocks < 1 || static_cast<int64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens > INT32_MAX) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: pool block count out of range");
     }
+    if ((pieces == nullptr) != (row_pieces == nullptr)) {
+        return pkv::fail(PKV_VALUE_ERROR, "decode attention: pieces and row_pieces must be given together");
+    }
     if ((reinterpret_cast<uintptr_t>(query) & 3) || (reinterpret_cast<uintptr_t>(out) & 3) ||
         query_stride % 2 || out_stride % 2 || (reinterpret_cast<uintptr_t>(pool) & 15) ||
-        (reinterpret_cast<uintptr_t>(workspace) & 15)) {
+        (reinterpret_cast<uintptr_t>(workspace) & 15) || (reinterpret_cast<uintptr_t>(pieces) & 15) ||
+        (reinterpret_cast<uintptr_t>(row_pieces) & 3)) {
         return pkv::fail(PKV_VALUE_ERROR, "decode attention: misaligned tensor");
     }
     if (grid > 1 && (workspace == nullptr || workspace_bytes < workspace_bytes_for(batch, grid))) {
@@ -949,7 +960,7 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.lengths = lengths;
     x.prefix = prefix;
     x.flat = flat;
-    x.cta_rows = cta_rows;
+    x.pieces = pieces;
     x.batch = batch;
     x.total_blocks = total_blocks;
     x.blocks_per_cta = blocks_per_cta;
@@ -961,6 +972,8 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.out_stride = out_stride;
     x.part_o = static_cast<float *>(workspace);
     x.part_ml = x.part_o ? x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
+    x.cta_ns = x.part_ml ? reinterpret_cast<unsigned *>(x.part_ml + (static_cast<int64_t>(batch) + grid) * kQueryHeads * 2)
+                         : nullptr;
     x.error_flag = error_flag;
     return PKV_OK;
 }
@@ -968,7 +981,8 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
 // Launch the split kernel, then (when rows can be split) the combine kernel
 // as its programmatic dependent on the same stream.
 template <bool FUSED>
-int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStream_t stream, const char *what) {
+int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, const int32_t *row_pieces,
+                cudaStream_t stream, const char *what) {
     cudaError_t e = launch_decode<FUSED>(grid, map, args, stream);
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string(what) + " launch failed: " + cudaGetErrorString(e));
     if (grid == 1) return PKV_OK;
@@ -986,7 +1000,7 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, cudaStr
     config.numAttrs = 1;
     const Partition partition{args.total_blocks, args.blocks_per_cta, args.big_ctas, args.tail_blocks};
     e = cudaLaunchKernelEx(&config, decode_combine_kernel, static_cast<const float *>(args.part_o),
-                           static_cast<const float *>(args.part_ml), args.prefix, args.batch, partition,
+                           static_cast<const float *>(args.part_ml), args.prefix, row_pieces, args.batch, partition,
                            args.out, args.out_stride);
     if (e != cudaSuccess) {
         return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
@@ -1006,40 +1020,29 @@ extern "C" int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_bloc
     DeviceInfo info;
     int rc = device_info(device, &info);
     if (rc) return rc;
+    // One piece per CTA slot (one wave), the blocks spread as evenly as
+    // integers allow: r pieces of q + 1 blocks, then grid - r pieces of q.
     const int64_t slots = static_cast<int64_t>(info.sms) * info.ctas_per_sm;
-    const int share = configured_big_share();
-    const int tail = configured_tail_blocks();
-    // Big pieces fill every CTA slot once; the rest goes to tail pieces.  A
-    // batch too small for pieces well above the tail size is split evenly.
-    const int64_t big_per_cta = static_cast<int64_t>(total_blocks) * share / (100 * slots);
-    int32_t grid, per_cta, big;
-    if (share < 100 && big_per_cta >= 2 * tail) {
-        per_cta = static_cast<int32_t>(big_per_cta);
-        big = static_cast<int32_t>(slots);
-        const int64_t split = static_cast<int64_t>(big) * per_cta;
-        grid = big + static_cast<int32_t>((total_blocks - split + tail - 1) / tail);
-    } else {
-        per_cta = static_cast<int32_t>((total_blocks + slots - 1) / slots);
-        grid = (total_blocks + per_cta - 1) / per_cta;
-        big = grid;
-    }
+    const int32_t grid = static_cast<int32_t>(std::min<int64_t>(slots, total_blocks));
+    const int32_t q = total_blocks / grid, r = total_blocks % grid;
     *out_grid = grid;
-    *out_blocks_per_cta = per_cta;
-    *out_big_ctas = big;
-    *out_tail_blocks = big == grid ? per_cta : tail;
+    *out_blocks_per_cta = r == 0 ? q : q + 1;
+    *out_big_ctas = r == 0 ? grid : r;
+    *out_tail_blocks = q;
     *out_workspace_bytes = workspace_bytes_for(batch, grid);
     return PKV_OK;
 }
 
 extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer,
                                     const void *query, int64_t query_stride, const int32_t *lengths,
-                                    const int32_t *prefix, const int32_t *flat, const int32_t *cta_rows,
-                                    int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                    const int32_t *prefix, const int32_t *flat, const int32_t *pieces,
+                                    const int32_t *row_pieces, int32_t batch, int32_t total_blocks, int32_t grid,
+                                    int32_t blocks_per_cta,
                                     int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
                                     void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
-    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, pieces, row_pieces, batch,
                            total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, workspace,
                            workspace_bytes, error_flag, &args);
     if (rc) return rc;
@@ -1049,19 +1052,20 @@ extern "C" int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_
     if ((rc = device_info(device, &info))) return rc;
     CUtensorMap map;
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
-    return launch_pass<false>(grid, map, args, static_cast<cudaStream_t>(stream), "decode attention");
+    return launch_pass<false>(grid, map, args, row_pieces, static_cast<cudaStream_t>(stream), "decode attention");
 }
 
 extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                 int64_t query_stride, const void *key, const void *value, int64_t kv_stride,
                                 const void *rope_table, const int32_t *lengths, const int32_t *prefix,
-                                const int32_t *flat, const int32_t *cta_rows, int32_t batch, int32_t total_blocks,
-                                int32_t grid, int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks,
+                                const int32_t *flat, const int32_t *pieces, const int32_t *row_pieces,
+                                int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
+                                int32_t big_ctas, int32_t tail_blocks,
                                 void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
                                 int32_t *error_flag, void *stream) {
     pkv::clear_error();
     LayerArgs args;
-    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+    int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, pieces, row_pieces, batch,
                            total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, workspace,
                            workspace_bytes, error_flag, &args);
     if (rc) return rc;
@@ -1083,7 +1087,7 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
     if ((rc = device_info(device, &info))) return rc;
     CUtensorMap map;
     if ((rc = pool_tensor_map(pool, num_blocks, &map))) return rc;
-    return launch_pass<true>(grid, map, args, static_cast<cudaStream_t>(stream), "decode layer");
+    return launch_pass<true>(grid, map, args, row_pieces, static_cast<cudaStream_t>(stream), "decode layer");
 }
 
 // ---------------------------------------------------------------------------
@@ -1160,7 +1164,8 @@ int noalloc_pool_map(const void *pool, int32_t num_blocks, CUtensorMap *map) {
 
 extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                             int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
-                                            const int32_t *flat, const int32_t *cta_rows, int32_t batch,
+                                            const int32_t *flat, const int32_t *pieces,
+                                            const int32_t *row_pieces, int32_t batch,
                                             int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
                                             int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
                                             int32_t *error_flag, void *stream) {
@@ -1179,11 +1184,12 @@ extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks
     int rc = noalloc_setup(device, &scratch);
     if (rc) return rc;
     LayerArgs args;
-    rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, cta_rows, batch,
+    rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, pieces, row_pieces, batch,
                        total_blocks, grid, blocks_per_cta, big_ctas, tail_blocks, out, out_stride, scratch,
                        kNoAllocScratchBytes, error_flag, &args);
     if (rc) return rc;
     CUtensorMap map;
     if ((rc = noalloc_pool_map(pool, num_blocks, &map))) return rc;
-    return launch_pass<false>(grid, map, args, static_cast<cudaStream_t>(stream), "no-alloc decode attention");
+    return launch_pass<false>(grid, map, args, row_pieces, static_cast<cudaStream_t>(stream),
+                              "no-alloc decode attention");
 }

@@ -9,6 +9,7 @@ missing or a tensor is not on a CUDA device: there is no non-native path.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -25,8 +26,9 @@ _PARTIAL_BYTES = _QUERY_HEADS * (_HEAD_DIM + 2) * 4  # one split partial: (m, l,
 
 
 def workspace_bytes(batch: int, grid: int) -> int:
-    """Workspace of a plan: one split partial per (row, piece) slot, batch + grid slots."""
-    return (batch + grid) * _PARTIAL_BYTES
+    """Workspace of a plan: a split partial per (row, piece) slot (batch + grid of
+    them), then four uint32 wall-time counters per CTA."""
+    return (batch + grid) * _PARTIAL_BYTES + grid * 16
 
 
 def _ptr(tensor: Tensor | None) -> ctypes.c_void_p:
@@ -151,6 +153,39 @@ class DecodePlan:
         return np.where(index < big, index * self.blocks_per_cta, big * self.blocks_per_cta + (index - big) * tail)
 
 
+# Row-switch cost of the decode kernel in blocks streamed (measured on B200);
+# the environment override is for tuning sweeps.
+ROW_COST = float(os.environ.get("PKV_DECODE_ROW_COST", "3.0"))
+
+
+def decode_tables(prefix: np.ndarray, grid: int, weights: np.ndarray | None = None,
+                  row_cost: float = ROW_COST) -> tuple[np.ndarray, np.ndarray]:
+    """Piece tables of a batch (host): pieces int32 [grid, 4], row_pieces int32 [B, 2].
+
+    ``prefix`` int32 [B + 1] (prefix[0] == 0); see pkv_decode_tables.
+    """
+    prefix = np.ascontiguousarray(prefix, dtype=np.int32)
+    batch = len(prefix) - 1
+    pieces = np.empty((grid, 4), dtype=np.int32)
+    row_pieces = np.empty((batch, 2), dtype=np.int32)
+    if weights is not None:
+        weights = np.ascontiguousarray(weights, dtype=np.float32)
+        if weights.shape != (grid,):
+            raise ValueError("weights must hold one value per piece")
+    check(
+        lib.pkv_decode_tables(
+            prefix.ctypes.data,
+            batch,
+            grid,
+            None if weights is None else weights.ctypes.data,
+            row_cost,
+            pieces.ctypes.data,
+            row_pieces.ctypes.data,
+        )
+    )
+    return pieces, row_pieces
+
+
 def decode_plan(device: torch.device, batch: int, total_blocks: int) -> DecodePlan:
     grid = ctypes.c_int32()
     per_cta = ctypes.c_int32()
@@ -185,7 +220,8 @@ def decode_attention(
     out: Tensor,
     workspace: Tensor | None,
     error_flag: Tensor,
-    cta_rows: Tensor | None = None,
+    pieces: Tensor | None = None,
+    row_pieces: Tensor | None = None,
 ) -> Tensor:
     """Split-K block-table attention of FP16 query [B, 32, 64] into ``out``."""
     device = pool.device
@@ -208,7 +244,8 @@ def decode_attention(
             _ptr(lengths),
             _ptr(prefix),
             _ptr(flat),
-            _ptr(cta_rows),
+            _ptr(pieces),
+            _ptr(row_pieces),
             batch,
             total_blocks,
             plan.grid,
@@ -240,7 +277,8 @@ def decode_layer(
     out: Tensor,
     workspace: Tensor | None,
     error_flag: Tensor,
-    cta_rows: Tensor | None = None,
+    pieces: Tensor | None = None,
+    row_pieces: Tensor | None = None,
 ) -> Tensor:
     """Fused decode layer of a staged batch: RoPE(Q, K), new-token KV write, attention.
 
@@ -273,7 +311,8 @@ def decode_layer(
             _ptr(lengths),
             _ptr(prefix),
             _ptr(flat),
-            _ptr(cta_rows),
+            _ptr(pieces),
+            _ptr(row_pieces),
             batch,
             total_blocks,
             plan.grid,

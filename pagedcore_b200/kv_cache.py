@@ -69,17 +69,21 @@ def allocate_kv_pool(config: PagedCoreConfig, *, device: str | torch.device = "c
 
 @dataclass(slots=True)
 class DecodeBatch:
-    """Device-resident block tables of a batch: what the attention kernel reads.
+    """Device-resident block tables of a batch: what the attention kernels read.
 
-    ``lengths`` [B], ``prefix`` [B+1] (cumulative block counts) and ``flat``
-    (the concatenated tables) are views of one int32 device buffer.
+    Views of one int32 device buffer, in this order: ``pieces`` [grid][4]
+    (begin, end, first row and its first block of each CTA's piece),
+    ``row_pieces`` [B][2] (first and last piece of each row), ``lengths``
+    [B], ``prefix`` [B+1] (cumulative block counts) and ``flat`` (the
+    concatenated block tables).
     """
 
     requests: tuple[RequestId, ...]
     lengths: Tensor
     prefix: Tensor
     flat: Tensor
-    cta_rows: Tensor  # [grid][2]: row holding the first block of each CTA's piece, and that row's first block
+    pieces: Tensor
+    row_pieces: Tensor
     total_blocks: int
     plan: kernels.DecodePlan
     host_lengths: np.ndarray
@@ -166,6 +170,18 @@ class _StepUploads:
         slot.released.record(self._compute)
 
 
+@dataclass(slots=True)
+class _SlotSpeeds:
+    """Per-CTA-slot weights of the decode pieces, from measured wall times."""
+
+    weights: np.ndarray  # float32 [grid], mean 1
+    updates: int = 0
+    pending: tuple | None = None  # (pinned counters [grid * 4], event) of a finished step
+
+
+_SPEED_UPDATES = 6  # weight updates before the weights freeze
+
+
 class KVAllocator:
     """Assign blocks within an existing CUDA pool (kv_cache.py:63-90).
 
@@ -173,7 +189,7 @@ class KVAllocator:
     stream current at construction.  Block reads borrow pool storage.
     """
 
-    def __init__(self, pool: Tensor, *, validation: str = "full") -> None:
+    def __init__(self, pool: Tensor, *, validation: str = "full", balance: str = "rows") -> None:
         if (
             pool.ndim != 6
             or pool.shape[:2] != (22, 2)
@@ -198,6 +214,14 @@ class KVAllocator:
         self._rope = device_table(pool.device)
         self._workspace: Tensor | None = None
         self._uploads = _StepUploads(pool.device, self._stream)
+        # How the decode pieces are cut: "rows" balances blocks plus row
+        # switches (a function of the batch only); "measured" also weights each
+        # CTA slot by its measured speed (slots on some SMs stream slower), the
+        # weights learnt over the first staged steps and then frozen.
+        if balance not in ("rows", "measured"):
+            raise ValueError("balance must be 'rows' or 'measured'")
+        self._balance = balance
+        self._speeds: dict[int, _SlotSpeeds] = {}
 
     # -- plumbing -------------------------------------------------------------
     @property
@@ -238,8 +262,57 @@ class KVAllocator:
         if nbytes <= 0:
             return None
         if self._workspace is None or self._workspace.numel() * 4 < nbytes:
-            self._workspace = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
+            self._workspace = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
         return self._workspace
+
+    # -- per-slot speed weights (balance="measured") ------------------------------
+    def _slot_counters(self, batch: int, plan: kernels.DecodePlan) -> Tensor | None:
+        """The workspace's [grid * 4] uint32 wall-time counters of this plan, as int32."""
+        workspace = self._workspace_for(plan.workspace_bytes)
+        if workspace is None:
+            return None
+        start = (batch + plan.grid) * kernels._PARTIAL_BYTES // 4
+        return workspace[start : start + 4 * plan.grid].view(torch.int32)
+
+    def _slot_weights(self, batch: int, plan: kernels.DecodePlan) -> np.ndarray | None:
+        if self._balance != "measured" or plan.grid < 2:
+            return None
+        state = self._speeds.get(plan.grid)
+        if state is None:
+            state = self._speeds[plan.grid] = _SlotSpeeds(np.ones(plan.grid, dtype=np.float32))
+            counters = self._slot_counters(batch, plan)
+            if counters is not None:
+                counters.zero_()  # the first measured step starts from zero
+        if state.pending is not None and state.pending[1].query():
+            counters = state.pending[0].numpy().astype(np.uint32).reshape(plan.grid, 4)
+            seconds = counters.max(axis=1).astype(np.float64)
+            state.pending = None
+            if seconds.min() > 0:
+                # Give a slot more work the sooner it finished (damped), mean 1.
+                step = (seconds.mean() / seconds) ** 0.7
+                weights = np.clip(state.weights * step, 0.5, 2.0)
+                state.weights = (weights / weights.mean()).astype(np.float32)
+                state.updates += 1
+        return state.weights
+
+    def _measure_slots(self, batch: int, plan: kernels.DecodePlan) -> None:
+        """After a staged step: copy out and clear its slot counters while calibrating."""
+        if self._balance != "measured" or plan.grid < 2:
+            return
+        state = self._speeds.get(plan.grid)
+        counters = self._slot_counters(batch, plan)
+        if state is None or counters is None or state.updates >= _SPEED_UPDATES or state.pending is not None:
+            return
+        host = torch.empty(counters.shape, dtype=torch.int32, pin_memory=True)
+        host.copy_(counters, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(self._stream)
+        counters.zero_()
+        state.pending = (host, done)
+
+    def slot_weights(self) -> dict[int, np.ndarray]:
+        """The measured per-slot weights by grid size (balance="measured")."""
+        return {grid: state.weights.copy() for grid, state in self._speeds.items()}
 
     def check_device_errors(self) -> None:
         """Synchronise and raise if a kernel flagged an out-of-range block or position."""
@@ -338,8 +411,8 @@ class KVAllocator:
         try:
             # The staged view (every row with its new token) is what the fused
             # decode layer reads; its tables travel with the slots in one copy.
-            host, total, plan, cta_rows = self._batch_tables(request_ids, handles, _VIEW_STAGED)
-            device, upload = self._uploads.upload((slots, positions, host, cta_rows))
+            tables, total, plan = self._batch_tables(request_ids, handles, _VIEW_STAGED)
+            device, upload = self._uploads.upload((tables, slots, positions))
         except BaseException:
             self._ledger.decode_abort()
             raise
@@ -347,10 +420,10 @@ class KVAllocator:
             requests=request_ids,
             handles=handles,
             rows={request_id: row for row, request_id in enumerate(request_ids)},
-            slots=device[:count],
-            positions=device[count : 2 * count],
+            slots=device[len(tables) : len(tables) + count],
+            positions=device[len(tables) + count :],
             host_positions=positions,
-            staged_batch=self._device_batch(request_ids, host, total, plan, device[2 * count :]),
+            staged_batch=self._device_batch(request_ids, tables, total, plan, device[: len(tables)]),
         )
         try:
             yield
@@ -359,6 +432,7 @@ class KVAllocator:
             raise
         else:
             self._ledger.decode_commit()
+            self._measure_slots(count, plan)
         finally:
             self._staged = None
             self._uploads.release(upload)
@@ -472,13 +546,12 @@ class KVAllocator:
         fixed = staged.launch_args
         if fixed is None:
             fixed = staged.launch_args = self._decode_layer_args(self.staged_decode_batch(), count)
-        pool_ptr, num_blocks, rope, lengths, prefix, flat, cta_rows, total, grid, per_cta, big, tail, ws, ws_bytes, err, stream = (
-            fixed
-        )
+        pool_ptr, num_blocks, rope, lengths, prefix, flat, pieces, row_pieces, total, grid, per_cta, big, tail, ws, ws_bytes, \
+            err, stream = fixed
         check(
             lib.pkv_decode_layer(
                 pool_ptr, num_blocks, layer, query.data_ptr(), query.stride(0), key.data_ptr(), value.data_ptr(),
-                key.stride(0), rope, lengths, prefix, flat, cta_rows, count, total, grid, per_cta, big, tail,
+                key.stride(0), rope, lengths, prefix, flat, pieces, row_pieces, count, total, grid, per_cta, big, tail,
                 out.data_ptr(), out.stride(0), ws, ws_bytes, err, stream,
             )
         )
@@ -491,7 +564,8 @@ class KVAllocator:
         workspace = self._workspace_for(batch.plan.workspace_bytes)
         return (
             self._pool.data_ptr(), self._pool.shape[2], self._rope.data_ptr(), batch.lengths.data_ptr(),
-            batch.prefix.data_ptr(), batch.flat.data_ptr(), batch.cta_rows.data_ptr(), batch.total_blocks,
+            batch.prefix.data_ptr(), batch.flat.data_ptr(), batch.pieces.data_ptr(), batch.row_pieces.data_ptr(),
+            batch.total_blocks,
             batch.plan.grid, batch.plan.blocks_per_cta, *batch.plan.pieces(),
             0 if workspace is None else workspace.data_ptr(),
             0 if workspace is None else workspace.numel() * 4, self._error.data_ptr(), self._stream.cuda_stream,
@@ -579,8 +653,13 @@ class KVAllocator:
 
     def _batch_tables(
         self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int
-    ) -> tuple[np.ndarray, int, kernels.DecodePlan, np.ndarray]:
-        """Host tables of a batch at ``layer``: [lengths | prefix | flat], blocks, plan, cta_rows."""
+    ) -> tuple[np.ndarray, int, kernels.DecodePlan]:
+        """Host tables of a batch at ``layer`` in upload order, its block count and plan.
+
+        Order: pieces [grid][4] | row_pieces [B][2] | lengths [B] | prefix [B+1]
+        | flat; the pieces come first so the kernel's 16-byte loads of them
+        are aligned.
+        """
         count = len(request_ids)
         if count == 0:
             raise ValueError("attention requires a nonempty batch")
@@ -591,31 +670,34 @@ class KVAllocator:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
         plan = kernels.decode_plan(self._pool.device, count, total)
-        prefix = host[count : 2 * count + 1]
-        rows = np.searchsorted(prefix, plan.piece_starts(), side="right") - 1
-        cta_rows = np.stack((rows, prefix[rows]), axis=1).astype(np.int32).reshape(-1)
-        return host[: 2 * count + 1 + total], total, plan, cta_rows
+        weights = self._slot_weights(count, plan)
+        pieces, row_pieces = kernels.decode_tables(host[count : 2 * count + 1], plan.grid, weights)
+        tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), host[: 2 * count + 1 + total]))
+        return tables, total, plan
 
     @staticmethod
     def _device_batch(
-        request_ids: tuple[RequestId, ...], host: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor
+        request_ids: tuple[RequestId, ...], tables: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor
     ) -> DecodeBatch:
-        """A DecodeBatch over ``device`` = [lengths | prefix | flat | cta_rows] as uploaded."""
-        count, used = len(request_ids), len(host)
+        """A DecodeBatch over ``device``, the uploaded copy of ``tables``."""
+        count = len(request_ids)
+        rows = 4 * plan.grid
+        start = rows + 2 * count
         return DecodeBatch(
             requests=request_ids,
-            lengths=device[:count],
-            prefix=device[count : 2 * count + 1],
-            flat=device[2 * count + 1 : used],
-            cta_rows=device[used:],
+            pieces=device[:rows],
+            row_pieces=device[rows:start],
+            lengths=device[start : start + count],
+            prefix=device[start + count : start + 2 * count + 1],
+            flat=device[start + 2 * count + 1 : start + 2 * count + 1 + total],
             total_blocks=total,
             plan=plan,
-            host_lengths=host[:count].copy(),
+            host_lengths=tables[start : start + count].copy(),
         )
 
     def _upload_batch(self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int) -> DecodeBatch:
-        host, total, plan, cta_rows = self._batch_tables(request_ids, handles, layer)
-        return self._device_batch(request_ids, host, total, plan, self._upload_i32(host, cta_rows))
+        tables, total, plan = self._batch_tables(request_ids, handles, layer)
+        return self._device_batch(request_ids, tables, total, plan, self._upload_i32(tables))
 
     def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
         """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""
@@ -634,6 +716,7 @@ class KVAllocator:
             out,
             self._workspace_for(batch.plan.workspace_bytes),
             self._error,
-            batch.cta_rows,
+            batch.pieces,
+            batch.row_pieces,
         )
         return out

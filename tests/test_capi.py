@@ -43,7 +43,7 @@ def test_device_entry_points_reject_bad_arguments_before_any_launch() -> None:
     status = _lib.lib.pkv_append_kv(None, 1, 0, 1, None, None, 0, 0, None, None, 1, None, None, None, 0, 0, None, None)
     assert status == _lib.PKV_VALUE_ERROR
     status = _lib.lib.pkv_decode_attention(
-        None, 1, 0, None, 0, None, None, None, None, 1, 1, 1, 1, 1, 1, None, 0, None, 0, None, None
+        None, 1, 0, None, 0, None, None, None, None, None, 1, 1, 1, 1, 1, 1, None, 0, None, 0, None, None
     )
     assert status == _lib.PKV_VALUE_ERROR
     assert b"null pointer" in _lib.lib.pkv_last_error()
@@ -55,7 +55,7 @@ def test_decode_entry_points_reject_a_partition_that_does_not_cover_the_blocks()
     fake = 1 << 20
     for grid, ok in ((12, False), (15, False), (14, True)):
         status = _lib.lib.pkv_decode_attention(
-            fake, 64, 0, fake, 2048, fake, fake, fake, None, 4, 100, grid, 8, 10, 5, fake, 2048, None, 0, fake, None
+            fake, 64, 0, fake, 2048, fake, fake, fake, None, None, 4, 100, grid, 8, 10, 5, fake, 2048, None, 0, fake, None
         )
         if ok:
             # The plan passes; the missing workspace is the next thing refused.

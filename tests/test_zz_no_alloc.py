@@ -33,7 +33,8 @@ def _noalloc(allocator: KVAllocator, batch, query: torch.Tensor, layer: int, out
         batch.lengths.data_ptr(),
         batch.prefix.data_ptr(),
         batch.flat.data_ptr(),
-        batch.cta_rows.data_ptr(),
+        batch.pieces.data_ptr(),
+        batch.row_pieces.data_ptr(),
         len(batch.requests),
         batch.total_blocks,
         batch.plan.grid,
@@ -76,7 +77,7 @@ def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row() -> None:
         kernels.decode_attention(allocator.pool, layer, query, batch.lengths, batch.prefix, batch.flat,
                                  batch.total_blocks, batch.plan, expected,
                                  allocator._workspace_for(batch.plan.workspace_bytes), allocator._error,
-                                 batch.cta_rows)
+                                 batch.pieces, batch.row_pieces)
         actual = torch.full_like(query, float("nan"))
         assert _noalloc(allocator, batch, query, layer, actual) == _lib.PKV_OK, _lib.lib.pkv_last_error()
         torch.cuda.synchronize()
@@ -86,10 +87,10 @@ def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row() -> None:
 
 def test_noalloc_entry_rejects_batches_beyond_its_fixed_array() -> None:
     # Refused on the host before any launch: the plan's partials must fit in 8 MiB
-    # ((batch + grid) * 8448 bytes).
+    # ((batch + grid) * 8448 + grid * 16 bytes).
     cuda_device()
     status = _lib.lib.pkv_decode_attention_noalloc(
-        None, 1, 0, None, 0, None, None, None, None, 990, 1000, 10, 100, 10, 100, None, 0, None, None
+        None, 1, 0, None, 0, None, None, None, None, None, 990, 1000, 10, 100, 10, 100, None, 0, None, None
     )
     assert status == _lib.PKV_VALUE_ERROR
     assert b"over the static scratch limit of 8388608" in _lib.lib.pkv_last_error()
