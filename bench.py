@@ -161,6 +161,8 @@ def _config(n_gpus: int) -> dict:
         "parallelism": f"dp{n_gpus} (independent sequences, one KV pool per GPU, no collective)",
         "pieces": "one per CTA slot, cut to balance blocks + row switches, weighted by each slot's measured speed "
                   f"(KVAllocator balance='measured', learnt in {CALIBRATION_STEPS} untimed setup steps, then frozen)",
+        "launch": "each step's 22 decode-layer launches (split + combine) replayed as CUDA graphs (DecodeStepGraph), "
+                  "captured during setup",
     }
 
 
@@ -195,7 +197,7 @@ def _bind_host_cores(device: int) -> str:
         import pynvml
 
         pynvml.nvmlInit()
-        handle = ClockSampler(device)._handle(pynvml)
+        handle = _nvml_handle(pynvml, device)
         words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
         cores = {64 * w + b for w, mask in enumerate(words) for b in range(64) if mask >> b & 1}
         cores &= set(range(os.cpu_count()))
@@ -207,67 +209,92 @@ def _bind_host_cores(device: int) -> str:
         return f"unbound ({error})"
 
 
+def _nvml_handle(pynvml, device: int):
+    """NVML handle of CUDA device `device` (matched by PCI bus id when torch reports it)."""
+    import torch
+
+    props = torch.cuda.get_device_properties(device)
+    bus = getattr(props, "pci_bus_id", None)
+    if bus is not None:
+        domain = getattr(props, "pci_domain_id", 0)
+        slot = getattr(props, "pci_device_id", 0)
+        try:
+            return pynvml.nvmlDeviceGetHandleByPciBusId(f"{domain:08x}:{bus:02x}:{slot:02x}.0")
+        except pynvml.NVMLError:
+            pass
+    return pynvml.nvmlDeviceGetHandleByIndex(device)
+
+
+def _sample_clocks(bus_id: str | None, index: int, period: float, ready, stop, sink) -> None:
+    """Child process: NVML SM clock and throttle reasons every `period` s until `stop`."""
+    samples, max_mhz, error = [], None, None
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id) if bus_id else pynvml.nvmlDeviceGetHandleByIndex(index)
+        except pynvml.NVMLError:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+        max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        ready.set()
+        while not stop.is_set():
+            samples.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
+                            int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+            stop.wait(period)
+    except Exception as exc:  # noqa: BLE001 - clocks are reported, never required
+        error = f"NVML unavailable: {exc}"
+        ready.set()
+    sink.send((samples, max_mhz, error))
+
+
 class ClockSampler:
-    """SM clock and throttle-reason samples (NVML, read-only) every 2 ms of the timed region."""
+    """SM clock and throttle-reason samples (NVML, read-only) every 2 ms of the timed region.
+
+    Sampled in a separate (spawned) process, so the sampling never competes
+    with the launching thread for the interpreter lock.
+    """
 
     # NVML clock-event reason bits.
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
+    PERIOD = 0.002
 
     def __init__(self, device: int) -> None:
         self.device = device
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
         self.error = None
-        self._stop = None
-        self._thread = None
+        self._child = None
 
-    def _handle(self, pynvml):
+    def __enter__(self) -> "ClockSampler":
+        import multiprocessing as mp
+
         import torch
 
         props = torch.cuda.get_device_properties(self.device)
         bus = getattr(props, "pci_bus_id", None)
-        if bus is not None:
-            domain = getattr(props, "pci_domain_id", 0)
-            slot = getattr(props, "pci_device_id", 0)
-            try:
-                return pynvml.nvmlDeviceGetHandleByPciBusId(f"{domain:08x}:{bus:02x}:{slot:02x}.0")
-            except pynvml.NVMLError:
-                pass
-        return pynvml.nvmlDeviceGetHandleByIndex(self.device)
-
-    def __enter__(self) -> "ClockSampler":
-        import threading
-
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            handle = self._handle(pynvml)
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
-        except Exception as error:  # noqa: BLE001 - clocks are reported, never required
-            self.error = f"NVML unavailable: {error}"
-            return self
-        self._stop = threading.Event()
-
-        def run() -> None:
-            while not self._stop.is_set():
-                try:
-                    mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
-                    reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))
-                    self.samples.append((mhz, reasons))
-                except Exception as error:  # noqa: BLE001
-                    self.error = str(error)
-                    return
-                self._stop.wait(0.002)
-
-        self._thread = threading.Thread(target=run, daemon=True)
-        self._thread.start()
+        bus_id = None if bus is None else (f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:"
+                                           f"{getattr(props, 'pci_device_id', 0):02x}.0")
+        ctx = mp.get_context("spawn")
+        self._ready, self._stop = ctx.Event(), ctx.Event()
+        self._receive, send = ctx.Pipe(duplex=False)
+        self._child = ctx.Process(target=_sample_clocks,
+                                  args=(bus_id, self.device, self.PERIOD, self._ready, self._stop, send), daemon=True)
+        self._child.start()
+        if not self._ready.wait(timeout=120):
+            self.error = "clock sampler did not start"
         return self
 
     def __exit__(self, *exc) -> None:
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
+        if self._child is None:
+            return
+        self._stop.set()
+        if self._receive.poll(30):
+            self.samples, self.max_mhz, error = self._receive.recv()
+            self.error = self.error or error
+        else:
+            self.error = self.error or "clock sampler returned nothing"
+        self._child.join(timeout=10)
 
     def summary(self) -> dict:
         reasons = set()
@@ -280,7 +307,7 @@ class ClockSampler:
             "sm_max_mhz": self.max_mhz,
             "samples": len(self.samples),
             "reasons": sorted(reasons),
-            "source": "NVML every 2 ms during the timed region",
+            "source": "NVML every 2 ms during the timed region, in a separate process",
         }
         if self.error:
             summary["error"] = self.error
@@ -307,6 +334,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     from pagedcore_b200 import workloads
     from pagedcore_b200.attention import paged_decode_attention
     from pagedcore_b200.engine_types import KVReservation, RequestId
+    from pagedcore_b200.graph import DecodeStepGraph
     from pagedcore_b200.kv_cache import KVAllocator
 
     total_steps = args.warmup + args.steps
@@ -347,11 +375,12 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     out = torch.empty(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device)
     stream = torch.cuda.current_stream(device)
 
+    # Each step's 22 fused decode-layer launches (+ combines) replay as one CUDA
+    # graph per (upload buffer, input buffer set); warm-up captures them all.
+    engine = DecodeStepGraph(allocator, requests)
+
     def step(q, k, v, dst=None) -> None:
-        dst = out if dst is None else dst
-        with allocator.append_decode(requests):
-            for layer in range(LAYERS):
-                allocator.decode_layer(layer, q[layer], k[layer], v[layer], out=dst[layer])
+        engine.step(q, k, v, out if dst is None else dst)
 
     def barrier() -> None:
         if world > 1:

@@ -109,6 +109,10 @@ int pkv_ledger_decode_check(pkv_ledger *ledger, int64_t request, int32_t layer,
                             int32_t *out_slot, int32_t *out_position);
 /* Record that `layer` was written (kv_cache.py:246); request == -1: all rows. */
 int pkv_ledger_decode_mark(pkv_ledger *ledger, int64_t request, int32_t layer);
+/* Record layers first .. first+count-1 as written for every staged row, each
+ * row's next layer being `first` (the checks of pkv_ledger_decode_check, once;
+ * for a step whose launches were enqueued together, e.g. as a CUDA graph). */
+int pkv_ledger_decode_mark_layers(pkv_ledger *ledger, int32_t first, int32_t count);
 /* Commit needs all 22 layers written (kv_cache.py:208-217); both commit and
  * abort leave no staged state behind. */
 int pkv_ledger_decode_commit(pkv_ledger *ledger);

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_ledger_decode_begin": (c_int, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
     "pkv_ledger_decode_check": (c_int, [c_void_p, c_int64, c_int32, i32p, i32p]),
     "pkv_ledger_decode_mark": (c_int, [c_void_p, c_int64, c_int32]),
+    "pkv_ledger_decode_mark_layers": (c_int, [c_void_p, c_int32, c_int32]),
     "pkv_ledger_decode_commit": (c_int, [c_void_p]),
     "pkv_ledger_decode_abort": (None, [c_void_p]),
     "pkv_ledger_decode_active": (c_int, [c_void_p]),

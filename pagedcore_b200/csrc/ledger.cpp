@@ -475,6 +475,21 @@ int pkv_ledger_decode_mark(pkv_ledger *L, int64_t request, int32_t layer) {
     return PKV_OK;
 }
 
+int pkv_ledger_decode_mark_layers(pkv_ledger *L, int32_t first, int32_t count) {
+    pkv::clear_error();
+    int rc = audit(L);
+    if (rc) return rc;
+    if (!L->staging) return fail(PKV_RUNTIME_ERROR, "decode writes require a staged append");
+    if (count < 1 || first < 0 || first + count > kLayers) {
+        return fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
+    }
+    for (int32_t row = 0; row < static_cast<int32_t>(L->staged_requests.size()); ++row) {
+        if ((rc = decode_row_check(L, row, first))) return rc;
+    }
+    for (auto &w : L->staged_written) w = first + count;
+    return PKV_OK;
+}
+
 void pkv_ledger_decode_abort(pkv_ledger *L) {
     L->staging = false;
     L->staged_requests.clear();

@@ -101,6 +101,7 @@ class _Staged:
     batch: DecodeBatch | None = None
     staged_batch: DecodeBatch | None = None  # staged view of every row, for decode_layer
     launch_args: tuple | None = None  # fixed pkv_decode_layer arguments of this step
+    flat_capacity: int = 0  # room of the flat block list in the step's upload buffer (a bound on total)
 
 
 @dataclass(slots=True)
@@ -134,15 +135,16 @@ class _StepUploads:
         # Growing: no copy or kernel may still use the old buffers.
         torch.cuda.synchronize(self._device)
         size = max(count, 2 * self._slots[0].host.numel() if self._slots else 8192)
-        self._slots = [
-            _UploadSlot(
-                torch.empty(size, dtype=torch.int32, pin_memory=True),
-                torch.empty(size, dtype=torch.int32, device=self._device),
-                torch.cuda.Event(),
-                torch.cuda.Event(),
-            )
-            for _ in range(2)
-        ]
+        with torch.inference_mode(False):  # persistent buffers, updated in place in any mode
+            self._slots = [
+                _UploadSlot(
+                    torch.empty(size, dtype=torch.int32, pin_memory=True),
+                    torch.empty(size, dtype=torch.int32, device=self._device),
+                    torch.cuda.Event(),
+                    torch.cuda.Event(),
+                )
+                for _ in range(2)
+            ]
         self._next = 0
 
     def upload(self, arrays: Sequence[np.ndarray]) -> tuple[Tensor, _UploadSlot]:
@@ -210,7 +212,8 @@ class KVAllocator:
         self._handles: dict[RequestId, int] = {}
         self._next_handle = 1
         self._staged: _Staged | None = None
-        self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
+        with torch.inference_mode(False):  # zeroed in place after a device error, in any mode
+            self._error = torch.zeros(1, dtype=torch.int32, device=pool.device)
         self._rope = device_table(pool.device)
         self._workspace: Tensor | None = None
         self._uploads = _StepUploads(pool.device, self._stream)
@@ -262,7 +265,8 @@ class KVAllocator:
         if nbytes <= 0:
             return None
         if self._workspace is None or self._workspace.numel() * 4 < nbytes:
-            self._workspace = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
+            with torch.inference_mode(False):  # persistent, updated in place in any mode
+                self._workspace = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=self._pool.device)
         return self._workspace
 
     # -- per-slot speed weights (balance="measured") ------------------------------
@@ -424,6 +428,7 @@ class KVAllocator:
             positions=device[len(tables) + count :],
             host_positions=positions,
             staged_batch=self._device_batch(request_ids, tables, total, plan, device[: len(tables)]),
+            flat_capacity=upload.device.numel() - (4 * plan.grid + 4 * count + 1),
         )
         try:
             yield

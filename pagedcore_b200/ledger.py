@@ -109,6 +109,10 @@ class BlockLedger:
     def decode_mark(self, request: int, layer: int) -> None:
         check(lib.pkv_ledger_decode_mark(self._handle, request, layer))
 
+    def decode_mark_layers(self, first: int, count: int) -> None:
+        """Record layers first..first+count-1 written for every staged row."""
+        check(lib.pkv_ledger_decode_mark_layers(self._handle, first, count))
+
     def decode_commit(self) -> None:
         check(lib.pkv_ledger_decode_commit(self._handle))
 

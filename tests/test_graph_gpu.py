@@ -1,0 +1,78 @@
+"""A staged decode step replayed as a CUDA graph (pagedcore_b200.graph).
+
+The graph launches exactly the kernels ``decode_layer`` launches, with the
+same tables, so outputs and pool bytes match the per-layer path bit for bit,
+over steps that alternate the upload buffers and the caller's buffer sets.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from pagedcore_b200 import workloads
+from pagedcore_b200.engine_types import KVReservation, RequestId
+from pagedcore_b200.graph import DecodeStepGraph
+from pagedcore_b200.kv_cache import KVAllocator
+from tests.conftest import cuda_device
+
+pytestmark = pytest.mark.gpu
+
+
+def twin_allocators(lengths, device):
+    need = sum(-(-(n + 12) // 16) for n in lengths) + 4
+    requests = tuple(RequestId(f"g{i}") for i in range(len(lengths)))
+    out = []
+    for _ in range(2):
+        pool = torch.full((22, 2, need, 16, 4, 64), torch.nan, dtype=torch.float16, device=device)
+        allocator = KVAllocator(pool, validation="incremental")
+        generator = torch.Generator(device=device).manual_seed(21)
+        for request, length in zip(requests, lengths, strict=True):
+            allocator.create(KVReservation(request, -(-(length + 12) // 16)))
+            kv = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+            allocator.append(request, kv, kv * 0.5)
+        out.append(allocator)
+    return out, requests
+
+
+def test_graph_steps_match_per_layer_launches_bit_for_bit() -> None:
+    device = cuda_device()
+    lengths = workloads.decode_lengths(21, 40, high=1500).tolist()
+    (graphed, plain), requests = twin_allocators(lengths, device)
+    count = len(lengths)
+    generator = torch.Generator(device=device).manual_seed(22)
+    sets = [
+        tuple(torch.randn(22, count, h, 64, dtype=torch.float16, device=device, generator=generator) for h in (32, 4, 4))
+        for _ in range(2)
+    ]
+    outs = [torch.empty(22, count, 32, 64, dtype=torch.float16, device=device) for _ in range(2)]
+    engine = DecodeStepGraph(graphed, requests)
+    for step in range(6):
+        which = (step // 2) % 2  # with the alternating upload buffers: all four pairs
+        q, k, v = sets[which]
+        out_graph = outs[which]
+        out_graph.fill_(float("nan"))
+        engine.step(q, k, v, out_graph)
+        out_plain = torch.empty_like(out_graph)
+        with plain.append_decode(requests):
+            for layer in range(22):
+                plain.decode_layer(layer, q[layer], k[layer], v[layer], out=out_plain[layer])
+        torch.cuda.synchronize()
+        assert torch.equal(out_graph, out_plain), step
+    assert engine.captures == 4  # two upload buffers x two caller buffer sets
+    assert torch.equal(graphed.pool.view(torch.int16), plain.pool.view(torch.int16))
+    assert [graphed.cached_length(r) for r in requests] == [n + 6 for n in lengths]
+    assert graphed.capacity() == plain.capacity()
+    graphed.check_device_errors()
+    plain.check_device_errors()
+
+
+def test_graph_step_rejects_buffers_of_the_wrong_shape() -> None:
+    device = cuda_device()
+    (allocator, _), requests = twin_allocators([5, 30], device)
+    engine = DecodeStepGraph(allocator, requests)
+    q = torch.zeros(22, 2, 32, 64, dtype=torch.float16, device=device)
+    kv = torch.zeros(22, 2, 4, 64, dtype=torch.float16, device=device)
+    with pytest.raises(ValueError, match="key must be"):
+        engine.step(q, kv[:, :1], kv, torch.empty_like(q))
+    assert [allocator.cached_length(r) for r in requests] == [5, 30]

@@ -509,3 +509,23 @@ def test_randomized_operations_match_oracle(blocks: int) -> None:
 
 def test_ceil_helper() -> None:
     assert [workloads.blocks_for(n) for n in (1, 16, 17)] == [math.ceil(n / 16) for n in (1, 16, 17)]
+
+
+def test_marking_a_run_of_layers_at_once_checks_like_one_by_one() -> None:
+    ledger = BlockLedger(8)
+    ledger.reserve(1, 2)
+    ledger.append(1, 5)
+    ledger.reserve(2, 2)
+    ledger.append(2, 16)
+    with pytest.raises(RuntimeError, match="staged append"):
+        ledger.decode_mark_layers(0, 22)
+    ledger.decode_begin([1, 2])
+    with pytest.raises(ValueError, match="in order"):
+        ledger.decode_mark_layers(1, 3)
+    with pytest.raises(ValueError, match="22 decoder layers"):
+        ledger.decode_mark_layers(20, 3)
+    ledger.decode_mark_layers(0, 10)
+    ledger.decode_check(-1, 10)
+    ledger.decode_mark_layers(10, 12)
+    ledger.decode_commit()
+    assert ledger.length(1) == 6 and ledger.length(2) == 17
