@@ -575,6 +575,72 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def run_stress_arm(args: argparse.Namespace) -> None:
+    """BASELINE config 5 (pagedcore_b200.stress): sustained decode under allocator churn."""
+    import torch
+    import torch.distributed as dist
+
+    from pagedcore_b200.stress import NEW_PROMPT, ROWS, StressRun, pool_blocks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    _bind_host_cores(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    run = StressRun(device, seed=5 + 1000 * rank)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    with ClockSampler(local_rank) as clocks:
+        result = run.run(args.stress_warmup, args.stress_iterations)
+    totals = torch.tensor([result.seconds, result.decode_tokens, result.attention_bytes], dtype=torch.float64,
+                          device=device)
+    if world > 1:
+        seconds = totals[:1].clone()
+        dist.all_reduce(seconds, op=dist.ReduceOp.MAX)
+        dist.all_reduce(totals, op=dist.ReduceOp.SUM)
+        totals[0] = seconds[0]
+    seconds, tokens, attention_bytes = totals.tolist()
+    if rank == 0:
+        peak, peak_kind = _peak_hbm()
+        line = {
+            "metric": "sustained decode tokens/s under allocator churn (BASELINE config 5)",
+            "value": tokens / seconds,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.stress_iterations,
+            "warmup": args.stress_warmup,
+            "ms_per_step": 1000.0 * seconds / args.stress_iterations,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded prompts, finish steps and K/V/Q)",
+            "config": {
+                "workload": f"config 5 per GPU: {ROWS} sequences reserving full 2048-token contexts, pool of "
+                            f"{pool_blocks()} blocks (90 % of their need), each finishing at a seeded step and "
+                            f"replaced by a {NEW_PROMPT}-token prompt; strict FIFO credit admission, one prefill "
+                            "write per iteration, one fused decode step per iteration for every active sequence",
+                "parallelism": f"dp{world} (independent sequences, one KV pool per GPU)",
+            },
+            "attn_gbs": attention_bytes / seconds / 1e9,
+            "attn_frac_of_peak": attention_bytes / seconds / 1e9 / peak,
+            "peak_kind": peak_kind,
+            "rank0": {"decode_tokens": result.decode_tokens, "prefill_tokens": result.prefill_tokens,
+                      "admitted": result.admitted, "completed": result.completed,
+                      "active_mean": result.active_mean},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -584,12 +650,18 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
+    parser.add_argument("--workload", choices=("decode", "stress"), default="decode",
+                        help="decode: config 4 (the headline line); stress: config 5 (allocator churn)")
+    parser.add_argument("--stress-iterations", type=int, default=300)
+    parser.add_argument("--stress-warmup", type=int, default=200)
     args = parser.parse_args()
     globals()["SEQUENCES"] = args.sequences
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload == "stress":
+        run_stress_arm(args)
     else:
         run_gpu_arm(args)
 

@@ -716,14 +716,28 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
     float M = -INFINITY, L = 0.f, A0 = 0.f, A1 = 0.f;
-    for (int c = cta_first; c <= cta_last; ++c) {
-        const int64_t idx = (static_cast<int64_t>(row) + c) * kQueryHeads + head;
-        const float2 ml = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
-        const float2 v = *reinterpret_cast<const float2 *>(part_o + idx * kHeadDim + 2 * lane);
-        const MergeWeights w = merge_weights(M, ml.x);
-        L = merge_value(L, ml.y, w);
-        A0 = merge_value(A0, v.x, w);
-        A1 = merge_value(A1, v.y, w);
+    // Pieces in order, four at a time: all four partials are loaded before
+    // any is merged, so a row costs about one L2 round trip per four pieces.
+    constexpr int kBatch = 4;
+    for (int c0 = cta_first; c0 <= cta_last; c0 += kBatch) {
+        float2 ml[kBatch], v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (c0 + j <= cta_last) {
+                const int64_t idx = (static_cast<int64_t>(row) + c0 + j) * kQueryHeads + head;
+                ml[j] = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
+                v[j] = *reinterpret_cast<const float2 *>(part_o + idx * kHeadDim + 2 * lane);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (c0 + j <= cta_last) {
+                const MergeWeights w = merge_weights(M, ml[j].x);
+                L = merge_value(L, ml[j].y, w);
+                A0 = merge_value(A0, v[j].x, w);
+                A1 = merge_value(A1, v[j].y, w);
+            }
+        }
     }
     *reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + 2 * lane) =
         __floats2half2_rn(__fdiv_rn(A0, L), __fdiv_rn(A1, L));
