@@ -95,6 +95,40 @@ def prefill_paged(
     return logits
 
 
+@torch.inference_mode()
+def prefill_paged_fused(
+    input_ids: Tensor, weights: TinyLlamaWeights, allocator: KVAllocator, request_id: RequestId
+) -> Tensor:
+    """Prefill a prompt chunk through the pool; return its logits [1, T, V].
+
+    Unlike ``prefill_paged`` nothing dense is kept: per layer the chunk's K
+    (rotated in the write) and V go straight to their pool slots, and the
+    causal attention reads them back through the block table with the
+    split-K decode kernel (token t of the chunk is a row of length
+    start + t + 1).  The request may already hold a cache (the chunk continues
+    it).  Attention accumulates in FP32 as paged decode does, so logits match
+    the dense FP16 prefill within tolerance, not bit for bit.  Positions are
+    published only after the whole forward succeeds.
+    """
+    _check_prompt(input_ids, weights)
+    if len(weights.layers) != LAYERS:
+        raise ValueError("paged prefill requires 22 decoder layers")
+    tokens = input_ids.shape[1]
+    with allocator.prefill_append(request_id, tokens) as chunk:
+        hidden = F.embedding(input_ids, weights.embedding)  # [1, T, 2048]
+        for index, layer in enumerate(weights.layers):
+            x = rms_norm(hidden, layer.input_norm)
+            query = F.linear(x, layer.q_proj).view(tokens, QUERY_HEADS, HEAD_DIM)
+            key = F.linear(x, layer.k_proj).view(tokens, KV_HEADS, HEAD_DIM)
+            value = F.linear(x, layer.v_proj).view(tokens, KV_HEADS, HEAD_DIM)
+            rotated = chunk.write_layer(index, key, value, query)
+            attention = chunk.attend(index, rotated)
+            hidden = hidden + F.linear(attention.view(1, tokens, HIDDEN), layer.o_proj)
+            hidden = hidden + swiglu(rms_norm(hidden, layer.post_attention_norm), layer)
+        logits = final_logits(hidden, weights)
+    return logits
+
+
 def _check_decode(input_ids: Tensor, weights: TinyLlamaWeights, request_ids: Sequence[RequestId]) -> None:
     if input_ids.dtype != torch.int64 or input_ids.ndim != 2 or input_ids.shape != (len(request_ids), 1):
         raise ValueError("input_ids must be int64 [batch, 1] matching request IDs")

@@ -172,6 +172,38 @@ class _StepUploads:
         slot.released.record(self._compute)
 
 
+class PrefillAppend:
+    """One planned prompt chunk of ``KVAllocator.prefill_append``."""
+
+    def __init__(self, allocator: KVAllocator, batch: DecodeBatch, slots: Tensor, positions: Tensor,
+                 tokens: int) -> None:
+        self._allocator = allocator
+        self.batch = batch
+        self.slots = slots
+        self.positions = positions
+        self.tokens = tokens
+
+    @torch.inference_mode()
+    def write_layer(self, layer: int, key: Tensor, value: Tensor, query: Tensor) -> Tensor:
+        """Rotate K and write K/V [T, 4, 64] at `layer`; return Q [T, 32, 64] rotated."""
+        allocator = self._allocator
+        allocator._check_worker()
+        if type(layer) is not int or not 0 <= layer < _LAYERS:
+            raise ValueError("layer_index must identify one of the 22 decoder layers")
+        rotated = torch.empty((1, self.tokens, 32, 64), dtype=torch.float16, device=allocator._pool.device)
+        kernels.append_kv(
+            allocator._pool, key.reshape(1, self.tokens, 4, 64), value.reshape(1, self.tokens, 4, 64), self.slots,
+            layer_begin=layer, error_flag=allocator._error, positions=self.positions, rope_table=allocator._rope,
+            query_in=query.reshape(1, self.tokens, 32, 64), query_out=rotated,
+        )
+        return rotated[0]
+
+    @torch.inference_mode()
+    def attend(self, layer: int, query: Tensor, out: Tensor | None = None) -> Tensor:
+        """Causal attention [T, 32, 64] of the rotated chunk queries at `layer` over the pool."""
+        return self._allocator.attend(self.batch, query, layer_index=layer, out=out)
+
+
 @dataclass(slots=True)
 class _SlotSpeeds:
     """Per-CTA-slot weights of the decode pieces, from measured wall times."""
@@ -389,6 +421,49 @@ class KVAllocator:
             meta = self._upload_i32(slots)
             kernels.append_kv(self._pool, key, value, meta, layer_begin=0, error_flag=self._error)
         # Publish valid positions only after both K and V writes were issued.
+        self._ledger.append_commit(handle, tokens)
+
+    @contextmanager
+    def prefill_append(self, request_id: RequestId, tokens: int) -> Iterator[PrefillAppend]:
+        """Append a prompt chunk layer by layer, attending to it through the pool.
+
+        Plans ``tokens`` new positions of ``request_id`` (blocks from the free
+        list as ``append`` would take them) and yields a :class:`PrefillAppend`
+        that writes one layer's K/V into those slots and computes that layer's
+        causal attention from the pool pages.  The positions are published when
+        the block exits without an error; otherwise nothing is published (the
+        written slots stay unowned).
+        """
+        self._check_worker()
+        if self._ledger.staging:
+            raise RuntimeError("KV mutation is not allowed during a staged decode append")
+        handle = self._handle(request_id)
+        self._call(self._ledger.length, request_id, handle)
+        if type(tokens) is not int or tokens < 1:
+            raise ValueError("a prompt chunk needs at least one token")
+        slots, start = self._call(self._ledger.append_plan, request_id, handle, tokens)
+        existing = self._ledger.table(handle)
+        # Physical block of every 16-token block of the extended context.
+        blocks = np.asarray(
+            [existing[j] if j < len(existing) else slots[16 * j - start] // 16
+             for j in range(-(-(start + tokens) // 16))],
+            dtype=np.int32,
+        )
+        # Token t of the chunk (position start + t) attends to positions 0..start+t.
+        lengths = np.arange(start + 1, start + tokens + 1, dtype=np.int32)
+        counts = -(-lengths // 16)
+        prefix = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+        total = int(prefix[-1])
+        flat = blocks[np.arange(total) - np.repeat(prefix[:-1], counts)]
+        plan = kernels.decode_plan(self._pool.device, tokens, total)
+        pieces, row_pieces = kernels.decode_tables(prefix, plan.grid)
+        tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), lengths, prefix, flat))
+        positions = np.arange(start, start + tokens, dtype=np.int32)
+        device = self._upload_i32(tables, slots, positions)
+        batch = self._device_batch((), tables, total, plan, device[: len(tables)], rows=tokens)
+        chunk = PrefillAppend(self, batch, device[len(tables) : len(tables) + tokens],
+                              device[len(tables) + tokens :], tokens)
+        yield chunk
         self._ledger.append_commit(handle, tokens)
 
     @contextmanager
@@ -682,16 +757,17 @@ class KVAllocator:
 
     @staticmethod
     def _device_batch(
-        request_ids: tuple[RequestId, ...], tables: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor
+        request_ids: tuple[RequestId, ...], tables: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor,
+        rows: int | None = None,
     ) -> DecodeBatch:
-        """A DecodeBatch over ``device``, the uploaded copy of ``tables``."""
-        count = len(request_ids)
-        rows = 4 * plan.grid
-        start = rows + 2 * count
+        """A DecodeBatch over ``device``, the uploaded copy of ``tables`` (``rows`` rows, default one per request)."""
+        count = len(request_ids) if rows is None else rows
+        piece_words = 4 * plan.grid
+        start = piece_words + 2 * count
         return DecodeBatch(
             requests=request_ids,
-            pieces=device[:rows],
-            row_pieces=device[rows:start],
+            pieces=device[:piece_words],
+            row_pieces=device[piece_words:start],
             lengths=device[start : start + count],
             prefix=device[start + count : start + 2 * count + 1],
             flat=device[start + 2 * count + 1 : start + 2 * count + 1 + total],

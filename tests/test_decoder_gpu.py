@@ -220,7 +220,7 @@ def _teacher_forced(record, step_fn) -> tuple[float, int, list[int]]:
     return worst, agree, disagree
 
 
-@pytest.mark.parametrize("path", ["per_row", "batched"])
+@pytest.mark.parametrize("path", ["per_row", "batched", "paged_prefill"])
 def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
     record, weights = cfg3
     device = cuda_device()
@@ -228,7 +228,10 @@ def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
     request = RequestId("cfg3")
     allocator.create(KVReservation(request, 16))
     prompt = torch.tensor([record["prompt"]], dtype=torch.int64, device=device)
-    prompt_logits = prefill_paged(prompt, weights, allocator, request)[0, -1]
+    if path == "paged_prefill":
+        prompt_logits = decoder.prefill_paged_fused(prompt, weights, allocator, request)[0, -1]
+    else:
+        prompt_logits = prefill_paged(prompt, weights, allocator, request)[0, -1]
     engine = BatchedDecoder(weights)
     ids = record["greedy_ids"]
 
@@ -248,3 +251,67 @@ def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
     allocator.check_device_errors()
     allocator.release_all(request)
     assert allocator.capacity() == CapacityCounts(20, 20, 0, 0, 0, 0)
+
+
+# -- paged prefill through the pool (prefill_paged_fused) ------------------------
+def test_fused_paged_prefill_matches_the_dense_prefill(small) -> None:
+    device = cuda_device()
+    dense, fused = new_allocator(8, device), new_allocator(8, device)
+    request = RequestId("p")
+    for allocator in (dense, fused):
+        allocator.create(KVReservation(request, 4))
+    ids = small_prompt(49).to(device)
+    expected = prefill_paged(ids, small, dense, request)
+    got = decoder.prefill_paged_fused(ids, small, fused, request)
+    torch.testing.assert_close(got, expected, atol=LOGIT_TOL, rtol=LOGIT_TOL)
+    assert torch.equal(got.argmax(-1), expected.argmax(-1))
+    assert fused.block_table(request) == dense.block_table(request) and fused.cached_length(request) == 49
+    assert fused.capacity() == dense.capacity()
+    table = fused.block_table(request)
+    # Layer 0's K/V come from identical inputs: bit-exact; deeper layers within tolerance.
+    for layer, tol in ((0, 0.0), (21, 2e-2)):
+        for logical, physical in enumerate(table):
+            valid = min(16, 49 - 16 * logical)
+            torch.testing.assert_close(fused.pool[layer, :, physical, :valid], dense.pool[layer, :, physical, :valid],
+                                       atol=tol, rtol=tol)
+    fused.check_device_errors()
+
+
+def test_fused_paged_prefill_continues_a_cache_in_chunks(small) -> None:
+    # Prompt of 49 tokens prefilled as 20 + 29 must give the dense logits of positions 20..48.
+    device = cuda_device()
+    allocator = new_allocator(8, device)
+    request = RequestId("chunks")
+    allocator.create(KVReservation(request, 4))
+    ids = small_prompt(49).to(device)
+    full, _ = prefill(ids, small)
+    decoder.prefill_paged_fused(ids[:, :20], small, allocator, request)
+    second = decoder.prefill_paged_fused(ids[:, 20:], small, allocator, request)
+    torch.testing.assert_close(second[0], full[0, 20:], atol=LOGIT_TOL, rtol=LOGIT_TOL)
+    assert allocator.cached_length(request) == 49
+    allocator.check_device_errors()
+
+
+def test_failed_fused_prefill_publishes_nothing(small, monkeypatch) -> None:
+    device = cuda_device()
+    allocator = new_allocator(8, device)
+    request = RequestId("fails")
+    allocator.create(KVReservation(request, 4))
+    counts = allocator.capacity()
+    calls = 0
+    original = decoder.swiglu
+
+    def fail(*args, **kwargs):
+        nonlocal calls
+        calls += 1
+        if calls == 5:
+            raise RuntimeError("injected prefill failure")
+        return original(*args, **kwargs)
+
+    monkeypatch.setattr(decoder, "swiglu", fail)
+    with pytest.raises(RuntimeError, match="injected prefill failure"):
+        decoder.prefill_paged_fused(small_prompt(33).to(device), small, allocator, request)
+    assert allocator.cached_length(request) == 0 and allocator.capacity() == counts
+    monkeypatch.undo()
+    logits = decoder.prefill_paged_fused(small_prompt(33).to(device), small, allocator, request)
+    assert logits.shape == (1, 33, 31) and allocator.cached_length(request) == 33
