@@ -226,6 +226,13 @@ int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, co
                          int32_t tail_blocks, void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
                          int32_t *error_flag, void *stream);
 
+/* pkv_decode_layer flags.  PKV_DECODE_EARLY_KV: the kernel enqueued just
+ * before this call on `stream` writes no pool data of `layer` and none of the
+ * tables (lengths, prefix, flat, pieces, row_pieces); the split kernel then
+ * starts streaming K/V before that kernel completes (it is launched as a
+ * programmatic dependent either way). */
+#define PKV_DECODE_EARLY_KV 1
+
 /* One decode layer for a staged batch: the fused form of write_decode_layer
  * (kv_cache.py:221-246) + apply_rope on Q and K (dense.py:33-61) +
  * paged_attention (attention.py:14-53).  For every row b the new token sits
@@ -242,7 +249,7 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
                      const int32_t *lengths, const int32_t *prefix, const int32_t *flat, const int32_t *pieces,
                      const int32_t *row_pieces, int32_t batch, int32_t total_blocks, int32_t grid,
                      int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
-                     void *workspace, int64_t workspace_bytes, int32_t *error_flag, void *stream);
+                     void *workspace, int64_t workspace_bytes, int32_t *error_flag, int32_t flags, void *stream);
 
 /* pkv_decode_attention without any allocation.  No counterpart in the
  * reference: it is for callers that cannot allocate device memory for this

@@ -27,6 +27,8 @@ DEVICE_BAD_BLOCK = 1
 DEVICE_BAD_POSITION = 2
 DEVICE_WAIT_TIMEOUT = 4
 
+DECODE_EARLY_KV = 1
+
 LIBRARY_PATH: Path = _build.LIBRARY
 
 i32p = POINTER(c_int32)
@@ -117,6 +119,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # workspace
             c_int64,  # workspace_bytes
             c_void_p,  # error_flag
+            c_int32,  # flags
             c_void_p,  # stream
         ],
     ),

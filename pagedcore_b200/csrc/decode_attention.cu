@@ -118,6 +118,7 @@ struct LayerArgs {
     const int32_t *pieces;     // [grid][4]: begin, end, first row and that row's first block of each
                                // CTA's piece (or null: the Partition below, rows found by search)
     int32_t *error_flag;
+    int32_t early_kv;          // FUSED: start streaming K/V before the previous kernel completes
 };
 
 // The plan's partition of the flat block list into one contiguous piece per
@@ -381,9 +382,13 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
 
     // The kernel is launched as a programmatic dependent of whatever precedes
-    // it on the stream, so its launch overlaps that kernel's tail; nothing here
-    // touches memory before that kernel has completed and its writes are visible.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // it on the stream, so its launch overlaps that kernel's tail.  Normally
+    // nothing here touches memory before that kernel has completed and its
+    // writes are visible.  With early_kv the caller guarantees that kernel
+    // writes no pool data of this layer and none of the step's tables: the
+    // pieces, block ids and the first K/V boxes are then fetched before the
+    // wait, and everything else (queries, new tokens, outputs) after it.
+    if (!a.early_kv) asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint64_t started = pkv::global_timer_ns();
     int begin, end, row = 0, row_first = 0;
     if (a.pieces != nullptr) {
@@ -443,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
             ++next_fetch;
         }
     }
+    if (a.early_kv) asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // First row of the range (the largest b with prefix[b] <= begin) and its
     // first block: from the piece table, else a 32-way search.
@@ -713,6 +719,9 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
             cta_last = piece_of(partition, prefix[row + 1] - 1);
         }
     }
+    // The next split kernel (another layer) reads nothing this kernel writes
+    // before its own wait: let it launch now.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
     float M = -INFINITY, L = 0.f, A0 = 0.f, A1 = 0.f;
@@ -1076,7 +1085,7 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
                                 int32_t batch, int32_t total_blocks, int32_t grid, int32_t blocks_per_cta,
                                 int32_t big_ctas, int32_t tail_blocks,
                                 void *out, int64_t out_stride, void *workspace, int64_t workspace_bytes,
-                                int32_t *error_flag, void *stream) {
+                                int32_t *error_flag, int32_t flags, void *stream) {
     pkv::clear_error();
     LayerArgs args;
     int rc = common_checks(pool, num_blocks, layer, query, query_stride, lengths, prefix, flat, pieces, row_pieces, batch,
@@ -1095,6 +1104,8 @@ extern "C" int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, c
     args.new_stride = kv_stride;
     args.rope_cos = static_cast<const __half *>(rope_table);
     args.rope_sin = args.rope_cos + PKV_CONTEXT_LIMIT * kRopeHalf;
+    if (flags & ~PKV_DECODE_EARLY_KV) return pkv::fail(PKV_VALUE_ERROR, "decode layer: unknown flags");
+    args.early_kv = (flags & PKV_DECODE_EARLY_KV) != 0;
     int device = 0;
     cudaGetDevice(&device);
     DeviceInfo info;

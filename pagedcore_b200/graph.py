@@ -22,7 +22,7 @@ from collections.abc import Sequence
 import torch
 from torch import Tensor
 
-from pagedcore_b200._lib import check, lib
+from pagedcore_b200._lib import DECODE_EARLY_KV, check, lib
 from pagedcore_b200.engine_types import RequestId
 from pagedcore_b200.kv_cache import KVAllocator
 
@@ -73,7 +73,10 @@ class DecodeStepGraph:
                     lib.pkv_decode_layer(
                         pool, num_blocks, layer, q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0),
                         rope, lengths, prefix, flat, pieces, row_pieces, count, bound, grid, per_cta, big, tail,
-                        o.data_ptr(), o.stride(0), ws, ws_bytes, err, side.cuda_stream,
+                        # Layers after the first follow this graph's own combine, which
+                        # writes no pool data: they may start streaming early.
+                        o.data_ptr(), o.stride(0), ws, ws_bytes, err, DECODE_EARLY_KV if layer else 0,
+                        side.cuda_stream,
                     )
                 )
         allocator._stream.wait_stream(side)

@@ -323,6 +323,7 @@ def decode_layer(
             _ptr(workspace),
             0 if workspace is None else workspace.numel() * workspace.element_size(),
             _ptr(error_flag),
+            0,  # flags
             _stream(pool.device),
         )
     )

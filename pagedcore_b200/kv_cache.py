@@ -632,7 +632,7 @@ class KVAllocator:
             lib.pkv_decode_layer(
                 pool_ptr, num_blocks, layer, query.data_ptr(), query.stride(0), key.data_ptr(), value.data_ptr(),
                 key.stride(0), rope, lengths, prefix, flat, pieces, row_pieces, count, total, grid, per_cta, big, tail,
-                out.data_ptr(), out.stride(0), ws, ws_bytes, err, stream,
+                out.data_ptr(), out.stride(0), ws, ws_bytes, err, 0, stream,
             )
         )
         self._ledger.decode_mark(-1, layer)
