@@ -237,6 +237,9 @@ def _sample_clocks(bus_id: str | None, index: int, period: float, ready, stop, s
         except pynvml.NVMLError:
             handle = pynvml.nvmlDeviceGetHandleByIndex(index)
         max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        # First calls can be slow: make them before the timed region starts.
+        pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
         ready.set()
         while not stop.is_set():
             samples.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
@@ -595,8 +598,9 @@ def run_stress_arm(args: argparse.Namespace) -> None:
     run = StressRun(device, seed=5 + 1000 * rank)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
+    run.warm(args.stress_warmup)
     with ClockSampler(local_rank) as clocks:
-        result = run.run(args.stress_warmup, args.stress_iterations)
+        result = run.run(0, args.stress_iterations)
     totals = torch.tensor([result.seconds, result.decode_tokens, result.attention_bytes], dtype=torch.float64,
                           device=device)
     if world > 1:
@@ -625,6 +629,9 @@ def run_stress_arm(args: argparse.Namespace) -> None:
                             f"{pool_blocks()} blocks (90 % of their need), each finishing at a seeded step and "
                             f"replaced by a {NEW_PROMPT}-token prompt; strict FIFO credit admission, one prefill "
                             "write per iteration, one fused decode step per iteration for every active sequence",
+                "launch": "each decode step's 22 decode-layer launches replayed as one CUDA graph (DecodeStepGraph "
+                          f"with {ROWS} rows: padded step tables, so one graph serves every batch)",
+                "warmup": f"{args.stress_warmup} untimed iterations before the timed ones",
                 "parallelism": f"dp{world} (independent sequences, one KV pool per GPU)",
             },
             "attn_gbs": attention_bytes / seconds / 1e9,

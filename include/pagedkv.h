@@ -186,7 +186,10 @@ int pkv_append_kv(void *pool, int32_t num_blocks, int32_t layer_begin, int32_t l
  * cut into one contiguous piece per CTA: big_ctas pieces of blocks_per_cta
  * blocks, then grid - big_ctas pieces of tail_blocks blocks (the last piece
  * may be shorter); big_ctas == grid is the uniform split.  Also returns the
- * bytes of split partials the caller must provide as workspace. */
+ * bytes of workspace the caller must provide: the first 16 * grid bytes hold
+ * four uint32 wall-time counters per CTA (nanoseconds each warp ran, added to
+ * on every launch, never cleared by the library), the rest the split
+ * partials. */
 int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
                     int32_t *out_blocks_per_cta, int32_t *out_big_ctas, int32_t *out_tail_blocks,
                     int64_t *out_workspace_bytes);

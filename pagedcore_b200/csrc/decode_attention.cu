@@ -920,8 +920,9 @@ cudaError_t launch_decode(int grid, const CUtensorMap &map, const LayerArgs &arg
     }
 }
 
-// Split partials of (batch + grid) (row, piece) slots, then each CTA's four
-// warp wall-time counters.
+// Each CTA's four warp wall-time counters first (CTA i's counters sit at the
+// same place whatever the launch shape), then the split partials of
+// (batch + grid) (row, piece) slots.
 int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
     return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float)) +
            static_cast<int64_t>(grid) * 4 * static_cast<int64_t>(sizeof(unsigned));
@@ -993,10 +994,11 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.layer = layer;
     x.out = static_cast<__half *>(out);
     x.out_stride = out_stride;
-    x.part_o = static_cast<float *>(workspace);
-    x.part_ml = x.part_o ? x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim : nullptr;
-    x.cta_ns = x.part_ml ? reinterpret_cast<unsigned *>(x.part_ml + (static_cast<int64_t>(batch) + grid) * kQueryHeads * 2)
-                         : nullptr;
+    if (workspace != nullptr) {
+        x.cta_ns = static_cast<unsigned *>(workspace);
+        x.part_o = reinterpret_cast<float *>(x.cta_ns + 4 * static_cast<int64_t>(grid));
+        x.part_ml = x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim;
+    }
     x.error_flag = error_flag;
     return PKV_OK;
 }

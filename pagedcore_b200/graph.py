@@ -6,12 +6,18 @@ cost about 37 us of Python and ctypes per layer on the host, close to the
 and replays them as one graph per step, so the host only stages the step
 (ledger, tables, one upload) and launches the graph.
 
-What a replay needs fixed is fixed: the pool, the workspace, the step
-tables' device buffers (the upload alternates between two, so a graph is
-kept per buffer), the caller's query/key/value/output buffers (a graph is
-kept per buffer set) and the number of pieces.  The block count changes
-every step; with piece tables the kernels use it only as a memory bound, so
-the graph is given the room of the flat list in its upload buffer.  The
+A replay repeats its launches' arguments, so nothing in them may depend on
+the step's batch.  The step is staged with a fixed layout
+(``append_decode(layout=(rows, pieces))``): its tables are padded to the
+graph's row capacity and to one piece per resident CTA slot, so the table
+addresses, the split grid (every slot; empty pieces exit at once) and the
+combine grid (every row; rows without pieces exit at once) are the same
+for every batch of up to ``rows`` requests.  The block count changes every
+step; with piece tables the kernels use it only as a memory bound, so the
+graph is given the room of the flat list in its upload buffer.  What stays
+fixed is the pool, the workspace, the upload buffer (the upload alternates
+between two, so a graph is kept per buffer) and the caller's
+query/key/value/output buffers (a graph is kept per buffer set).  The
 ledger records the 22 layers after each replay is enqueued.
 """
 
@@ -22,6 +28,7 @@ from collections.abc import Sequence
 import torch
 from torch import Tensor
 
+from pagedcore_b200 import kernels
 from pagedcore_b200._lib import DECODE_EARLY_KV, check, lib
 from pagedcore_b200.engine_types import RequestId
 from pagedcore_b200.kv_cache import KVAllocator
@@ -30,39 +37,51 @@ _LAYERS = 22
 
 
 class DecodeStepGraph:
-    """Decode steps of a fixed batch through captured CUDA graphs.
+    """Decode steps of up to ``rows`` requests through captured CUDA graphs.
 
-    ``step(query, key, value, out)`` does what ``append_decode`` plus
-    ``decode_layer`` for layers 0..21 do, with query [22, B, 32, 64] and
-    key/value [22, B, 4, 64] unrotated FP16 and out [22, B, 32, 64] FP16
-    written.  Graphs are captured on a side stream and replayed on the
-    allocator's stream.
+    ``step(query, key, value, out, request_ids)`` does what ``append_decode``
+    plus ``decode_layer`` for layers 0..21 do for ``request_ids`` (default:
+    the ids given at construction), with query [22, rows, 32, 64] and
+    key/value [22, rows, 4, 64] unrotated FP16 and out [22, rows, 32, 64]
+    FP16; row i of each belongs to the step's i-th request, and rows past the
+    batch are neither read nor written.  ``rows`` defaults to the number of
+    ids given at construction.  Graphs are captured on a side stream and
+    replayed on the allocator's stream.
     """
 
-    def __init__(self, allocator: KVAllocator, request_ids: Sequence[RequestId], *, max_graphs: int = 8) -> None:
+    def __init__(
+        self,
+        allocator: KVAllocator,
+        request_ids: Sequence[RequestId] = (),
+        *,
+        rows: int | None = None,
+        max_graphs: int = 8,
+    ) -> None:
         self.allocator = allocator
         self.requests = tuple(request_ids)
+        self.rows = len(self.requests) if rows is None else rows
+        if self.rows < 1 or len(self.requests) > self.rows:
+            raise ValueError("a decode step graph needs 1 <= len(request_ids) <= rows")
+        self.grid = kernels.decode_slots(allocator.pool.device)
         self.max_graphs = max_graphs
         self._graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
         self.captures = 0
 
     def _check(self, query: Tensor, key: Tensor, value: Tensor, out: Tensor) -> None:
-        count = len(self.requests)
         device = self.allocator.pool.device
         for name, tensor, heads in (("query", query, 32), ("key", key, 4), ("value", value, 4), ("out", out, 32)):
             if (
-                tensor.shape != (_LAYERS, count, heads, 64)
+                tensor.shape != (_LAYERS, self.rows, heads, 64)
                 or tensor.dtype != torch.float16
                 or tensor.device != device
                 or not tensor.is_contiguous()
             ):
-                raise ValueError(f"{name} must be contiguous FP16 [22, batch, {heads}, 64] on the pool device")
+                raise ValueError(f"{name} must be contiguous FP16 [22, {self.rows}, {heads}, 64] on the pool device")
 
     def _capture(self, args: tuple, query: Tensor, key: Tensor, value: Tensor, out: Tensor) -> torch.cuda.CUDAGraph:
         allocator = self.allocator
         (pool, num_blocks, rope, lengths, prefix, flat, pieces, row_pieces, bound, grid, per_cta, big, tail, ws,
          ws_bytes, err) = args
-        count = len(self.requests)
         side = torch.cuda.Stream(allocator.pool.device)
         side.wait_stream(allocator._stream)
         graph = torch.cuda.CUDAGraph()
@@ -72,7 +91,7 @@ class DecodeStepGraph:
                 check(
                     lib.pkv_decode_layer(
                         pool, num_blocks, layer, q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0),
-                        rope, lengths, prefix, flat, pieces, row_pieces, count, bound, grid, per_cta, big, tail,
+                        rope, lengths, prefix, flat, pieces, row_pieces, self.rows, bound, grid, per_cta, big, tail,
                         # Layers after the first follow this graph's own combine, which
                         # writes no pool data: they may start streaming early.
                         o.data_ptr(), o.stride(0), ws, ws_bytes, err, DECODE_EARLY_KV if layer else 0,
@@ -84,18 +103,22 @@ class DecodeStepGraph:
         return graph
 
     @torch.inference_mode()
-    def step(self, query: Tensor, key: Tensor, value: Tensor, out: Tensor) -> Tensor:
+    def step(
+        self, query: Tensor, key: Tensor, value: Tensor, out: Tensor,
+        request_ids: Sequence[RequestId] | None = None,
+    ) -> Tensor:
         allocator = self.allocator
+        requests = self.requests if request_ids is None else tuple(request_ids)
+        if not 1 <= len(requests) <= self.rows:
+            raise ValueError(f"a decode step graph serves 1 to {self.rows} requests, not {len(requests)}")
         self._check(query, key, value, out)
-        with allocator.append_decode(self.requests):
+        with allocator.append_decode(requests, layout=(self.rows, self.grid)):
             staged = allocator._staged
-            batch = staged.staged_batch
-            fixed = allocator._decode_layer_args(batch, len(self.requests))
-            grid = batch.plan.grid
+            fixed = allocator._decode_layer_args(staged.staged_batch, self.rows, self.grid)
             # With piece tables the kernels take the block count only as a
-            # bound and ignore the arithmetic partition: pass the step's upload
+            # bound and ignore the arithmetic partition: pass the upload's
             # room and constants, so the arguments repeat from step to step.
-            args = (*fixed[:8], staged.flat_capacity, grid, 1, grid, 1, *fixed[13:16])
+            args = (*fixed[:8], staged.flat_capacity, self.grid, 1, self.grid, 1, *fixed[13:16])
             cache_key = (args, query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr())
             graph = self._graphs.get(cache_key)
             if graph is None:

@@ -26,8 +26,8 @@ _PARTIAL_BYTES = _QUERY_HEADS * (_HEAD_DIM + 2) * 4  # one split partial: (m, l,
 
 
 def workspace_bytes(batch: int, grid: int) -> int:
-    """Workspace of a plan: a split partial per (row, piece) slot (batch + grid of
-    them), then four uint32 wall-time counters per CTA."""
+    """Workspace of a plan: four uint32 wall-time counters per CTA (the first
+    16 * grid bytes), then a split partial per (row, piece) slot (batch + grid)."""
     return (batch + grid) * _PARTIAL_BYTES + grid * 16
 
 
@@ -206,6 +206,11 @@ def decode_plan(device: torch.device, batch: int, total_blocks: int) -> DecodePl
         )
     )
     return DecodePlan(grid.value, per_cta.value, workspace.value, big.value, tail.value)
+
+
+def decode_slots(device: torch.device) -> int:
+    """The largest grid ``decode_plan`` chooses on ``device`` (resident CTA slots)."""
+    return decode_plan(device, 1, 1 << 24).grid
 
 
 def decode_attention(

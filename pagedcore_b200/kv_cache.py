@@ -302,21 +302,20 @@ class KVAllocator:
         return self._workspace
 
     # -- per-slot speed weights (balance="measured") ------------------------------
-    def _slot_counters(self, batch: int, plan: kernels.DecodePlan) -> Tensor | None:
-        """The workspace's [grid * 4] uint32 wall-time counters of this plan, as int32."""
+    def _slot_counters(self, plan: kernels.DecodePlan) -> Tensor | None:
+        """The plan's [grid * 4] uint32 wall-time counters (the workspace's first words), as int32."""
         workspace = self._workspace_for(plan.workspace_bytes)
         if workspace is None:
             return None
-        start = (batch + plan.grid) * kernels._PARTIAL_BYTES // 4
-        return workspace[start : start + 4 * plan.grid].view(torch.int32)
+        return workspace[: 4 * plan.grid].view(torch.int32)
 
-    def _slot_weights(self, batch: int, plan: kernels.DecodePlan) -> np.ndarray | None:
+    def _slot_weights(self, plan: kernels.DecodePlan) -> np.ndarray | None:
         if self._balance != "measured" or plan.grid < 2:
             return None
         state = self._speeds.get(plan.grid)
         if state is None:
             state = self._speeds[plan.grid] = _SlotSpeeds(np.ones(plan.grid, dtype=np.float32))
-            counters = self._slot_counters(batch, plan)
+            counters = self._slot_counters(plan)
             if counters is not None:
                 counters.zero_()  # the first measured step starts from zero
         if state.pending is not None and state.pending[1].query():
@@ -331,12 +330,12 @@ class KVAllocator:
                 state.updates += 1
         return state.weights
 
-    def _measure_slots(self, batch: int, plan: kernels.DecodePlan) -> None:
+    def _measure_slots(self, plan: kernels.DecodePlan) -> None:
         """After a staged step: copy out and clear its slot counters while calibrating."""
         if self._balance != "measured" or plan.grid < 2:
             return
         state = self._speeds.get(plan.grid)
-        counters = self._slot_counters(batch, plan)
+        counters = self._slot_counters(plan)
         if state is None or counters is None or state.updates >= _SPEED_UPDATES or state.pending is not None:
             return
         host = torch.empty(counters.shape, dtype=torch.int32, pin_memory=True)
@@ -467,8 +466,15 @@ class KVAllocator:
         self._ledger.append_commit(handle, tokens)
 
     @contextmanager
-    def append_decode(self, request_ids: tuple[RequestId, ...]) -> Iterator[None]:
-        """Stage one token per request; commit all 22 layers together (kv_cache.py:181-219)."""
+    def append_decode(
+        self, request_ids: tuple[RequestId, ...], *, layout: tuple[int, int] | None = None
+    ) -> Iterator[None]:
+        """Stage one token per request; commit all 22 layers together (kv_cache.py:181-219).
+
+        ``layout=(rows, pieces)`` pads the staged step's device tables to
+        ``rows`` rows and ``pieces`` pieces, so their addresses and a launch
+        over them do not depend on the batch (``DecodeStepGraph``).
+        """
         self._check_worker()
         if self._ledger.staging:
             raise RuntimeError("KV mutation is not allowed during a staged decode append")
@@ -490,11 +496,12 @@ class KVAllocator:
         try:
             # The staged view (every row with its new token) is what the fused
             # decode layer reads; its tables travel with the slots in one copy.
-            tables, total, plan = self._batch_tables(request_ids, handles, _VIEW_STAGED)
+            tables, total, plan = self._batch_tables(request_ids, handles, _VIEW_STAGED, layout)
             device, upload = self._uploads.upload((tables, slots, positions))
         except BaseException:
             self._ledger.decode_abort()
             raise
+        rows, grid = (count, plan.grid) if layout is None else layout
         self._staged = _Staged(
             requests=request_ids,
             handles=handles,
@@ -502,8 +509,8 @@ class KVAllocator:
             slots=device[len(tables) : len(tables) + count],
             positions=device[len(tables) + count :],
             host_positions=positions,
-            staged_batch=self._device_batch(request_ids, tables, total, plan, device[: len(tables)]),
-            flat_capacity=upload.device.numel() - (4 * plan.grid + 4 * count + 1),
+            staged_batch=self._device_batch(request_ids, tables, total, plan, device[: len(tables)], rows, grid),
+            flat_capacity=upload.device.numel() - (4 * grid + 4 * rows + 1),
         )
         try:
             yield
@@ -512,7 +519,7 @@ class KVAllocator:
             raise
         else:
             self._ledger.decode_commit()
-            self._measure_slots(count, plan)
+            self._measure_slots(plan)
         finally:
             self._staged = None
             self._uploads.release(upload)
@@ -625,7 +632,8 @@ class KVAllocator:
             raise ValueError("out must be FP16 [batch, 32, 64] with contiguous rows")
         fixed = staged.launch_args
         if fixed is None:
-            fixed = staged.launch_args = self._decode_layer_args(self.staged_decode_batch(), count)
+            batch = self.staged_decode_batch()
+            fixed = staged.launch_args = self._decode_layer_args(batch, count, batch.plan.grid)
         pool_ptr, num_blocks, rope, lengths, prefix, flat, pieces, row_pieces, total, grid, per_cta, big, tail, ws, ws_bytes, \
             err, stream = fixed
         check(
@@ -639,14 +647,15 @@ class KVAllocator:
         staged.written = layer + 1
         return out
 
-    def _decode_layer_args(self, batch: DecodeBatch, count: int) -> tuple:
-        """Launch arguments of pkv_decode_layer that stay fixed for a staged step."""
-        workspace = self._workspace_for(batch.plan.workspace_bytes)
+    def _decode_layer_args(self, batch: DecodeBatch, rows: int, grid: int) -> tuple:
+        """Launch arguments of pkv_decode_layer that stay fixed for a staged step launched over
+        ``rows`` rows and ``grid`` pieces (the batch's own, or its padded layout's)."""
+        workspace = self._workspace_for(kernels.workspace_bytes(rows, grid))
         return (
             self._pool.data_ptr(), self._pool.shape[2], self._rope.data_ptr(), batch.lengths.data_ptr(),
             batch.prefix.data_ptr(), batch.flat.data_ptr(), batch.pieces.data_ptr(), batch.row_pieces.data_ptr(),
             batch.total_blocks,
-            batch.plan.grid, batch.plan.blocks_per_cta, *batch.plan.pieces(),
+            grid, batch.plan.blocks_per_cta, *batch.plan.pieces(),
             0 if workspace is None else workspace.data_ptr(),
             0 if workspace is None else workspace.numel() * 4, self._error.data_ptr(), self._stream.cuda_stream,
         )
@@ -732,17 +741,23 @@ class KVAllocator:
         return batch
 
     def _batch_tables(
-        self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int
+        self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int,
+        layout: tuple[int, int] | None = None,
     ) -> tuple[np.ndarray, int, kernels.DecodePlan]:
         """Host tables of a batch at ``layer`` in upload order, its block count and plan.
 
         Order: pieces [grid][4] | row_pieces [B][2] | lengths [B] | prefix [B+1]
         | flat; the pieces come first so the kernel's 16-byte loads of them
-        are aligned.
+        are aligned.  With ``layout=(rows, pieces)`` the first four are padded
+        to ``pieces`` pieces and ``rows`` rows: empty pieces (0, 0, 0, 0), rows
+        with no pieces (0, 0), length 0 and prefix ``total``, which every
+        kernel skips.
         """
         count = len(request_ids)
         if count == 0:
             raise ValueError("attention requires a nonempty batch")
+        if layout is not None and count > layout[0]:
+            raise ValueError(f"a batch of {count} requests exceeds the layout's {layout[0]} rows")
         host = np.empty(2 * count + 1 + 129 * count, dtype=np.int32)
         try:
             total = self._ledger.batch_into(handles, layer, host)
@@ -750,19 +765,35 @@ class KVAllocator:
             missing = next((r for r in request_ids if r not in self._handles), None)
             raise KeyError(missing) from error
         plan = kernels.decode_plan(self._pool.device, count, total)
-        weights = self._slot_weights(count, plan)
+        weights = self._slot_weights(plan)
         pieces, row_pieces = kernels.decode_tables(host[count : 2 * count + 1], plan.grid, weights)
-        tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), host[: 2 * count + 1 + total]))
+        if layout is None:
+            tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), host[: 2 * count + 1 + total]))
+            return tables, total, plan
+        rows, grid = layout
+        if plan.grid > grid:
+            raise ValueError(f"the batch's plan needs {plan.grid} pieces; the layout has {grid}")
+        tables = np.zeros(4 * grid + 4 * rows + 1 + total, dtype=np.int32)
+        tables[: 4 * plan.grid] = pieces.reshape(-1)
+        at = 4 * grid
+        tables[at : at + 2 * count] = row_pieces.reshape(-1)
+        at += 2 * rows
+        tables[at : at + count] = host[:count]  # lengths
+        at += rows
+        tables[at : at + count + 1] = host[count : 2 * count + 1]  # prefix
+        tables[at + count + 1 : at + rows + 1] = total
+        tables[at + rows + 1 :] = host[2 * count + 1 : 2 * count + 1 + total]  # flat
         return tables, total, plan
 
     @staticmethod
     def _device_batch(
         request_ids: tuple[RequestId, ...], tables: np.ndarray, total: int, plan: kernels.DecodePlan, device: Tensor,
-        rows: int | None = None,
+        rows: int | None = None, grid: int | None = None,
     ) -> DecodeBatch:
-        """A DecodeBatch over ``device``, the uploaded copy of ``tables`` (``rows`` rows, default one per request)."""
+        """A DecodeBatch over ``device``, the uploaded copy of ``tables`` (``rows`` rows, default one per
+        request; ``grid`` pieces, default the plan's)."""
         count = len(request_ids) if rows is None else rows
-        piece_words = 4 * plan.grid
+        piece_words = 4 * (plan.grid if grid is None else grid)
         start = piece_words + 2 * count
         return DecodeBatch(
             requests=request_ids,

@@ -8,7 +8,8 @@ credits admit the next queued request, a 512-token prompt.  The worker loop is
 ``scheduler.Worker`` (strict FIFO, one prefill per iteration, one decode step
 for every active sequence); the prefill is a paged write of the prompt's K/V
 with RoPE (synthetic K/V: the KV path, not the dense model), the decode step
-one fused decode-layer launch per layer.  Reported: decode tokens/s over the
+the 22 fused decode-layer launches of ``DecodeStepGraph``, one CUDA graph
+replay whatever the active batch.  Reported: decode tokens/s over the
 timed iterations, the attention's algorithmic bytes per second, admissions
 and completions.
 """
@@ -21,6 +22,7 @@ import torch
 
 from pagedcore_b200 import workloads
 from pagedcore_b200.engine_types import RequestId
+from pagedcore_b200.graph import DecodeStepGraph
 from pagedcore_b200.kv_cache import KVAllocator
 from pagedcore_b200.scheduler import EOS_TOKEN, Request, Worker, required_blocks
 
@@ -68,6 +70,7 @@ class StressRun:
         self.q = torch.randn(LAYERS, rows, 32, 64, dtype=torch.float16, device=device, generator=generator)
         self.k = torch.randn(LAYERS, rows, 4, 64, dtype=torch.float16, device=device, generator=generator)
         self.out = torch.empty(LAYERS, rows, 32, 64, dtype=torch.float16, device=device)
+        self.graph = DecodeStepGraph(self.allocator, rows=rows)
         self.finish_at: dict[RequestId, int] = {}
         self.lengths: dict[RequestId, int] = {}
         self.next_id = 0
@@ -97,10 +100,7 @@ class StressRun:
     def _decode(self, batch) -> list[int]:
         count = len(batch)
         ids = tuple(request.request_id for request in batch)
-        with self.allocator.append_decode(ids):
-            for layer in range(LAYERS):
-                self.allocator.decode_layer(layer, self.q[layer, :count], self.k[layer, :count],
-                                            self.k[layer, :count], out=self.out[layer, :count])
+        self.graph.step(self.q, self.k, self.k, self.out, ids)
         tokens = []
         for request in batch:
             length = self.lengths[request.request_id] = self.lengths[request.request_id] + 1
@@ -118,10 +118,14 @@ class StressRun:
         for _ in range(len(self.worker.completed) - completed):
             self.submit(self.new_prompt)
 
-    def run(self, warmup: int, iterations: int) -> StressResult:
-        for _ in range(warmup):
+    def warm(self, iterations: int) -> None:
+        """Untimed iterations, then wait for the device."""
+        for _ in range(iterations):
             self.iterate()
         torch.cuda.synchronize(self.device)
+
+    def run(self, warmup: int, iterations: int) -> StressResult:
+        self.warm(warmup)
         base = (self.decode_tokens, self.prefill_tokens, self.attention_bytes, self.active_sum,
                 self.next_id - len(self.worker.pending), len(self.worker.completed))
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -7,6 +7,7 @@ over steps that alternate the upload buffers and the caller's buffer sets.
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -62,6 +63,38 @@ def test_graph_steps_match_per_layer_launches_bit_for_bit() -> None:
     assert engine.captures == 4  # two upload buffers x two caller buffer sets
     assert torch.equal(graphed.pool.view(torch.int16), plain.pool.view(torch.int16))
     assert [graphed.cached_length(r) for r in requests] == [n + 6 for n in lengths]
+    assert graphed.capacity() == plain.capacity()
+    graphed.check_device_errors()
+    plain.check_device_errors()
+
+
+def test_one_graph_serves_batches_of_every_size_and_order() -> None:
+    device = cuda_device()
+    lengths = workloads.decode_lengths(23, 40, high=1500).tolist()
+    (graphed, plain), requests = twin_allocators(lengths, device)
+    rows = len(requests)
+    generator = torch.Generator(device=device).manual_seed(24)
+    q, k, v = (torch.randn(22, rows, h, 64, dtype=torch.float16, device=device, generator=generator) for h in (32, 4, 4))
+    out_graph = torch.empty(22, rows, 32, 64, dtype=torch.float16, device=device)
+    engine = DecodeStepGraph(graphed, rows=rows)
+    order = np.random.default_rng(25)
+    for step, count in enumerate((rows, 1, 17, 33, 2, rows, 9, 40)):
+        chosen = tuple(requests[i] for i in order.permutation(rows)[:count])
+        out_graph.fill_(float("nan"))
+        engine.step(q, k, v, out_graph, chosen)
+        out_plain = torch.empty(22, count, 32, 64, dtype=torch.float16, device=device)
+        with plain.append_decode(chosen):
+            for layer in range(22):
+                plain.decode_layer(layer, q[layer, :count], k[layer, :count], v[layer, :count], out=out_plain[layer])
+        torch.cuda.synchronize()
+        assert torch.equal(out_graph[:, :count], out_plain), step
+        assert torch.isnan(out_graph[:, count:]).all(), step  # rows past the batch are not written
+    assert engine.captures == 2  # one per upload buffer, whatever the batch
+    assert torch.equal(graphed.pool.view(torch.int16), plain.pool.view(torch.int16))
+    assert [graphed.cached_length(r) for r in requests] == [plain.cached_length(r) for r in requests]
+    assert graphed.capacity() == plain.capacity()
+    with pytest.raises(ValueError, match="serves 1 to 40"):
+        engine.step(q, k, v, out_graph, requests + requests[:1])
     assert graphed.capacity() == plain.capacity()
     graphed.check_device_errors()
     plain.check_device_errors()
