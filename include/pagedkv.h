@@ -186,10 +186,14 @@ int pkv_append_kv(void *pool, int32_t num_blocks, int32_t layer_begin, int32_t l
  * cut into one contiguous piece per CTA: big_ctas pieces of blocks_per_cta
  * blocks, then grid - big_ctas pieces of tail_blocks blocks (the last piece
  * may be shorter); big_ctas == grid is the uniform split.  Also returns the
- * bytes of workspace the caller must provide: the first 16 * grid bytes hold
- * four uint32 wall-time counters per CTA (nanoseconds each warp ran, added to
- * on every launch, never cleared by the library), the rest the split
- * partials. */
+ * bytes of workspace the caller must provide, zeroed before its first use
+ * and otherwise left to the library: the first 2 KiB hold slot-claim
+ * counters (when the grid is one full wave of CTAs, each CTA takes the
+ * pieces assigned to the SM it runs on; every launch leaves these at zero),
+ * then 16 * grid bytes of four uint32 wall-time counters per piece
+ * (nanoseconds each warp ran, added to on every launch, never cleared by the
+ * library), then the split partials.  Launches that share a workspace must not overlap
+ * on the GPU. */
 int pkv_decode_plan(int32_t device, int32_t batch, int32_t total_blocks, int32_t *out_grid,
                     int32_t *out_blocks_per_cta, int32_t *out_big_ctas, int32_t *out_tail_blocks,
                     int64_t *out_workspace_bytes);
@@ -231,9 +235,11 @@ int pkv_decode_attention(const void *pool, int32_t num_blocks, int32_t layer, co
 
 /* pkv_decode_layer flags.  PKV_DECODE_EARLY_KV: the kernel enqueued just
  * before this call on `stream` writes no pool data of `layer` and none of the
- * tables (lengths, prefix, flat, pieces, row_pieces); the split kernel then
- * starts streaming K/V before that kernel completes (it is launched as a
- * programmatic dependent either way). */
+ * tables (lengths, prefix, flat, pieces, row_pieces), and if it is the second
+ * kernel of a decode launch on the same workspace, that launch was for a layer
+ * of the other parity (consecutive layers); the split kernel then claims its
+ * piece and starts streaming K/V before that kernel completes (it is launched
+ * as a programmatic dependent either way). */
 #define PKV_DECODE_EARLY_KV 1
 
 /* One decode layer for a staged batch: the fused form of write_decode_layer

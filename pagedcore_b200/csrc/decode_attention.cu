@@ -11,6 +11,12 @@
 // piece of it (the plan's Partition: normally [g*W, (g+1)*W)), which may
 // cover the tail of one row, whole short rows and the head of another, so
 // every CTA streams the same number of KV bytes whatever the ragged lengths.
+// With a piece table the host sizes the pieces (blocks, row switches, and the
+// measured speed of each slot), and when the grid is one full wave the CTAs
+// claim slots by the SM they run on (slot s * k + j is the j-th CTA on SM s):
+// the hardware places CTAs on SMs in a different order at every launch, while
+// an SM's speed stays the same from launch to launch, so only SM-bound slots
+// can be given work by speed.
 // Warp w of a CTA serves KV head w and its 8 query heads (GQA).
 //
 // Data movement - each warp runs its own TMA pipeline of STAGES stages: per
@@ -85,6 +91,12 @@ constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
 constexpr float kWeightShift = 15.0f;                       // P scaled by 2^15 before FP16
 constexpr int kPartialFloats = kQueryHeads * (kHeadDim + 2);
+// Slot claims: one counter per SM (up to kClaimWords SMs); two such sets,
+// used by layers of alternate parity.  The combine kernel zeroes a launch's
+// set once the split kernel has completed.
+constexpr int kClaimWords = 256;
+constexpr int kCombineThreads = 256;
+static_assert(kClaimWords <= kCombineThreads, "one combine CTA zeroes a claim set");
 
 template <int STAGES>
 constexpr int smem_bytes() {
@@ -115,6 +127,8 @@ struct LayerArgs {
     float *part_o;             // [(B + grid)][32][64]
     float *part_ml;            // [(B + grid)][32][2]
     unsigned *cta_ns;          // [grid][4]: each warp's wall time, accumulated over launches (or null)
+    int32_t *claims;           // [2][kClaimWords]: per-SM slot counters (or null)
+    int32_t sm_slots;          // > 0: CTAs take the slots of the SM they run on (sm_slots per SM)
     const int32_t *pieces;     // [grid][4]: begin, end, first row and that row's first block of each
                                // CTA's piece (or null: the Partition below, rows found by search)
     int32_t *error_flag;
@@ -373,26 +387,53 @@ __device__ __forceinline__ void write_output(const LayerArgs &a, int row, int he
     }
 }
 
-// Three 4-stage CTAs fit an SM's shared memory; the bound holds registers to
-// match (65536 / (3 * 128) = 170 per thread).
+// The slot of this CTA when slots are claimed per SM (warp 0, all lanes).
+// The pieces of SM s are slots s * k .. s * k + k - 1 (k = sm_slots), so the
+// work an SM gets, and the speed the host measures for a slot, belong to one
+// SM whatever order the hardware places the CTAs in.  A CTA takes the next
+// slot of its own SM; one that finds them all taken (an SM hosting more CTAs
+// than k) takes a slot left by another SM in one pass over the counters.
+// Counters only grow during a launch and there are as many slots as CTAs, so
+// every CTA gets exactly one: -1 means the counters were not zero at launch.
+__device__ __forceinline__ int claim_slot(const LayerArgs &a, int32_t *claims, int lane) {
+    const int k = a.sm_slots;
+    const int groups = static_cast<int>(gridDim.x) / k;
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    int slot = -1;
+    if (lane == 0 && smid < static_cast<unsigned>(groups)) {
+        const int c = atomicAdd(claims + smid, 1);
+        if (c < k) slot = static_cast<int>(smid) * k + c;
+    }
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    for (int base = 0; slot < 0 && base < groups; base += 32) {
+        const int s = base + lane;
+        const bool open = s < groups && *reinterpret_cast<volatile int32_t *>(claims + s) < k;
+        unsigned candidates = __ballot_sync(0xffffffffu, open);
+        while (candidates != 0 && slot < 0) {
+            const int pick = base + __ffs(candidates) - 1;
+            candidates &= candidates - 1;
+            int got = -1;
+            if (lane == 0) {
+                const int c = atomicAdd(claims + pick, 1);
+                if (c < k) got = pick * k + c;
+            }
+            slot = __shfl_sync(0xffffffffu, got, 0);
+        }
+    }
+    return slot;
+}
+
+// One CTA's piece: piece `slot` of the table (or of the partition).
 template <int STAGES, bool FUSED>
-__global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
-    decode_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ LayerArgs a) {
+__device__ __forceinline__ void decode_cta(const CUtensorMap &pool_map, const LayerArgs &a, const int slot,
+                                           const uint64_t started) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t barriers[kWarps * kMaxStages];
 
-    // The kernel is launched as a programmatic dependent of whatever precedes
-    // it on the stream, so its launch overlaps that kernel's tail.  Normally
-    // nothing here touches memory before that kernel has completed and its
-    // writes are visible.  With early_kv the caller guarantees that kernel
-    // writes no pool data of this layer and none of the step's tables: the
-    // pieces, block ids and the first K/V boxes are then fetched before the
-    // wait, and everything else (queries, new tokens, outputs) after it.
-    if (!a.early_kv) asm volatile("griddepcontrol.wait;" ::: "memory");
-    const uint64_t started = pkv::global_timer_ns();
     int begin, end, row = 0, row_first = 0;
     if (a.pieces != nullptr) {
-        const int4 piece = reinterpret_cast<const int4 *>(a.pieces)[blockIdx.x];
+        const int4 piece = reinterpret_cast<const int4 *>(a.pieces)[slot];
         begin = piece.x;
         end = piece.y;
         row = piece.z;
@@ -402,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
             return;
         }
     } else {
-        piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, blockIdx.x, begin, end);
+        piece_range(Partition{a.total_blocks, a.blocks_per_cta, a.big_ctas, a.tail_blocks}, slot, begin, end);
     }
     if (begin >= end) return;
 
@@ -675,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
         if (row_first >= begin && row_last <= end) {  // the whole row is in this CTA's piece
             write_output(a, row, head0, g, o, l0, l1);
         } else {  // merged by decode_combine_kernel
-            store_partial(a, static_cast<int64_t>(row) + blockIdx.x, head0, g, o, m0, l0, m1, l1);
+            store_partial(a, static_cast<int64_t>(row) + slot, head0, g, o, m0, l0, m1, l1);
         }
         if (!has_next || failed_range) break;
         ++row;
@@ -690,10 +731,49 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     for (int c = consumed; c < next_fetch - begin; ++c) {
         pkv::mbar_wait_bounded(bar0 + 8 * (c % STAGES), (c / STAGES) & 1, kWaitPolls);
     }
-    // The host may weight the pieces by each CTA slot's measured speed.
+    // The host may weight the pieces by each slot's measured speed.
     if (lane == 0 && a.cta_ns != nullptr) {
-        atomicAdd(&a.cta_ns[4 * blockIdx.x + warp], static_cast<unsigned>(pkv::global_timer_ns() - started));
+        atomicAdd(&a.cta_ns[4 * slot + warp], static_cast<unsigned>(pkv::global_timer_ns() - started));
     }
+}
+
+// Three 4-stage CTAs fit an SM's shared memory; the bound holds registers to
+// match (65536 / (3 * 128) = 170 per thread).
+template <int STAGES, bool FUSED>
+__global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
+    decode_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ LayerArgs a) {
+    __shared__ int claimed;
+    // The kernel is launched as a programmatic dependent of whatever precedes
+    // it on the stream, so its launch overlaps that kernel's tail.  Normally
+    // nothing here touches memory before that kernel has completed and its
+    // writes are visible.  With early_kv the caller guarantees that kernel
+    // writes no pool data of this layer and none of the step's tables: the
+    // slot claim, the piece, block ids and the first K/V boxes are then
+    // fetched before the wait, and everything else (queries, new tokens,
+    // outputs) after it.
+    //
+    // Claim counters: launch n's set is zeroed by its combine after launch
+    // n has completed, and the next launch may claim before that combine
+    // has run (early_kv), so consecutive launches use alternate sets (by
+    // layer parity).  Launch n's set is next used by launch n + 2, whose
+    // launch needs launch n + 1's signal, which launch n + 1 gives only after
+    // its griddepcontrol.wait, i.e. after launch n's combine has completed.
+    // (A launch without early_kv waits before claiming.)
+    if (!a.early_kv) asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint64_t started = pkv::global_timer_ns();
+    const int lane = threadIdx.x & 31;
+    int32_t *const claims = a.sm_slots > 0 ? a.claims + (a.layer & 1) * kClaimWords : nullptr;
+    int slot = static_cast<int>(blockIdx.x);
+    if (a.sm_slots > 0) {
+        if (threadIdx.x < 32) {
+            const int got = claim_slot(a, claims, lane);
+            if (lane == 0) claimed = got;
+        }
+        __syncthreads();
+        slot = claimed;
+        if (slot < 0 && threadIdx.x == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
+    }
+    if (slot >= 0) decode_cta<STAGES, FUSED>(pool_map, a, slot, started);
     // The combine kernel (launched as a programmatic dependent) may start.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -701,10 +781,10 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
 // Second pass: one warp per (row, query head) of a split row merges its
 // partials.  It is launched as a programmatic dependent of the split kernel,
 // so its launch and prologue overlap the split kernel's tail.
-__global__ void __launch_bounds__(256) decode_combine_kernel(
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
     const int32_t *__restrict__ prefix, const int32_t *__restrict__ row_pieces, int32_t batch, Partition partition,
-    __half *__restrict__ out, int64_t out_stride) {
+    __half *__restrict__ out, int64_t out_stride, int32_t *__restrict__ claims) {
     const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int row = pair / kQueryHeads;
@@ -723,6 +803,8 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(
     // before its own wait: let it launch now.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The split kernel has completed: its slot claims are done with.
+    if (claims != nullptr && blockIdx.x == 0 && threadIdx.x < kClaimWords) claims[threadIdx.x] = 0;
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
     float M = -INFINITY, L = 0.f, A0 = 0.f, A1 = 0.f;
     // Pieces in order, four at a time: all four partials are loaded before
@@ -920,12 +1002,15 @@ cudaError_t launch_decode(int grid, const CUtensorMap &map, const LayerArgs &arg
     }
 }
 
-// Each CTA's four warp wall-time counters first (CTA i's counters sit at the
-// same place whatever the launch shape), then the split partials of
-// (batch + grid) (row, piece) slots.
+// The slot claim counters first, then each slot's four warp wall-time
+// counters (both at the same place whatever the launch shape: launches of
+// other shapes write their partials after their own counters, never over the
+// claim counters, which must stay zero between launches), then the split
+// partials of (batch + grid) (row, piece) slots.
 int64_t workspace_bytes_for(int32_t batch, int32_t grid) {
-    return (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float)) +
-           static_cast<int64_t>(grid) * 4 * static_cast<int64_t>(sizeof(unsigned));
+    return 2 * kClaimWords * static_cast<int64_t>(sizeof(int32_t)) +
+           static_cast<int64_t>(grid) * 4 * static_cast<int64_t>(sizeof(unsigned)) +
+           (static_cast<int64_t>(batch) + grid) * kPartialFloats * static_cast<int64_t>(sizeof(float));
 }
 
 // The pieces of (grid, per_cta, big, tail) are nonempty and cover exactly
@@ -995,9 +1080,18 @@ int common_checks(const void *pool, int32_t num_blocks, int32_t layer, const voi
     x.out = static_cast<__half *>(out);
     x.out_stride = out_stride;
     if (workspace != nullptr) {
-        x.cta_ns = static_cast<unsigned *>(workspace);
+        x.claims = static_cast<int32_t *>(workspace);
+        x.cta_ns = reinterpret_cast<unsigned *>(x.claims + 2 * kClaimWords);
         x.part_o = reinterpret_cast<float *>(x.cta_ns + 4 * static_cast<int64_t>(grid));
         x.part_ml = x.part_o + (static_cast<int64_t>(batch) + grid) * kQueryHeads * kHeadDim;
+        // Per-SM slots when the pieces come from a table and the grid is one
+        // full wave of CTAs.
+        DeviceInfo info;
+        int device = 0;
+        if (pieces != nullptr && cudaGetDevice(&device) == cudaSuccess && device_info(device, &info) == PKV_OK &&
+            info.sms <= kClaimWords && grid == info.sms * info.ctas_per_sm) {
+            x.sm_slots = info.ctas_per_sm;
+        }
     }
     x.error_flag = error_flag;
     return PKV_OK;
@@ -1011,7 +1105,7 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, const i
     cudaError_t e = launch_decode<FUSED>(grid, map, args, stream);
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string(what) + " launch failed: " + cudaGetErrorString(e));
     if (grid == 1) return PKV_OK;
-    const int warps_per_cta = 8;
+    const int warps_per_cta = kCombineThreads / 32;
     const int pairs = args.batch * kQueryHeads;
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3((pairs + warps_per_cta - 1) / warps_per_cta);
@@ -1026,7 +1120,8 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, const i
     const Partition partition{args.total_blocks, args.blocks_per_cta, args.big_ctas, args.tail_blocks};
     e = cudaLaunchKernelEx(&config, decode_combine_kernel, static_cast<const float *>(args.part_o),
                            static_cast<const float *>(args.part_ml), args.prefix, row_pieces, args.batch, partition,
-                           args.out, args.out_stride);
+                           args.out, args.out_stride,
+                           args.sm_slots > 0 ? args.claims + (args.layer & 1) * kClaimWords : nullptr);
     if (e != cudaSuccess) {
         return pkv::fail(PKV_CUDA_ERROR, std::string("decode combine launch failed: ") + cudaGetErrorString(e));
     }

@@ -23,12 +23,15 @@ _KV_HEADS = 4
 _QUERY_HEADS = 32
 _HEAD_DIM = 64
 _PARTIAL_BYTES = _QUERY_HEADS * (_HEAD_DIM + 2) * 4  # one split partial: (m, l, O) of 32 heads, FP32
+_CLAIM_BYTES = 2 * 256 * 4  # two sets of per-SM slot-claim counters and a launch's exit count
 
 
 def workspace_bytes(batch: int, grid: int) -> int:
-    """Workspace of a plan: four uint32 wall-time counters per CTA (the first
-    16 * grid bytes), then a split partial per (row, piece) slot (batch + grid)."""
-    return (batch + grid) * _PARTIAL_BYTES + grid * 16
+    """Workspace of a plan: 2 x 256 int32 slot-claim counters (the first 2 KiB),
+    four uint32 wall-time counters per slot, then a split partial per (row,
+    piece) slot (batch + grid).  It must be zero before its first use; the
+    kernels leave the claim counters at zero."""
+    return _CLAIM_BYTES + grid * 16 + (batch + grid) * _PARTIAL_BYTES
 
 
 def _ptr(tensor: Tensor | None) -> ctypes.c_void_p:

@@ -303,11 +303,12 @@ class KVAllocator:
 
     # -- per-slot speed weights (balance="measured") ------------------------------
     def _slot_counters(self, plan: kernels.DecodePlan) -> Tensor | None:
-        """The plan's [grid * 4] uint32 wall-time counters (the workspace's first words), as int32."""
+        """The plan's [grid * 4] uint32 wall-time counters (after the claim counters), as int32."""
         workspace = self._workspace_for(plan.workspace_bytes)
         if workspace is None:
             return None
-        return workspace[: 4 * plan.grid].view(torch.int32)
+        start = kernels._CLAIM_BYTES // 4
+        return workspace[start : start + 4 * plan.grid].view(torch.int32)
 
     def _slot_weights(self, plan: kernels.DecodePlan) -> np.ndarray | None:
         if self._balance != "measured" or plan.grid < 2:

@@ -91,7 +91,7 @@ def test_fused_layer_matches_oracle_under_every_plan(pieces: tuple[int, int, int
         staged = allocator._staged
         batch = allocator._upload_batch(staged.requests, staged.handles, -2)
         plan = kernels.DecodePlan.split(count, batch.total_blocks, *pieces)
-        workspace = torch.empty(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
+        workspace = torch.zeros(plan.workspace_bytes // 4, dtype=torch.float32, device=device)
         for layer in range(22):
             allocator.ledger.decode_check(-1, layer)
             out = torch.empty(count, 32, 64, dtype=torch.float16, device=device)

@@ -27,7 +27,7 @@ def test_pieces_are_contiguous_nonempty_and_cover_every_block(total: int, pieces
     assert starts[0] == 0 and ends[-1] == total
     assert np.all(ends > starts)
     assert np.array_equal(starts[1:], ends[:-1])
-    assert plan.workspace_bytes == (9 + plan.grid) * _PARTIAL_BYTES + plan.grid * 16
+    assert plan.workspace_bytes == (9 + plan.grid) * _PARTIAL_BYTES + plan.grid * 16 + 2048
     big, tail = plan.pieces()
     sizes = ends - starts
     full = sizes[:-1]  # every piece but the last has its nominal size
@@ -43,7 +43,7 @@ def test_device_plan_is_a_valid_partition(batch: int, total: int) -> None:
     starts = plan.piece_starts()
     ends = piece_ends(plan, total)
     assert starts[0] == 0 and ends[-1] == total and np.all(ends > starts)
-    assert plan.workspace_bytes == (batch + plan.grid) * _PARTIAL_BYTES + plan.grid * 16
+    assert plan.workspace_bytes == (batch + plan.grid) * _PARTIAL_BYTES + plan.grid * 16 + 2048
     big, tail = plan.pieces()
     assert 1 <= big <= plan.grid and tail >= 1
 
