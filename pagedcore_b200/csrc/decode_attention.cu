@@ -778,17 +778,21 @@ __global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Second pass: one warp per (row, query head) of a split row merges its
-// partials.  It is launched as a programmatic dependent of the split kernel,
-// so its launch and prologue overlap the split kernel's tail.
+// Second pass: one warp per (row, pair of query heads) of a split row merges
+// its partials, 16 lanes per head and 4 dims per lane (two heads per warp
+// keep the grid to one wave of CTAs, so the kernel's signal to its own
+// dependents is not held back by CTAs waiting for room).  It is launched as a
+// programmatic dependent of the split kernel, so its launch and prologue
+// overlap the split kernel's tail.
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_ml,
     const int32_t *__restrict__ prefix, const int32_t *__restrict__ row_pieces, int32_t batch, Partition partition,
     __half *__restrict__ out, int64_t out_stride, int32_t *__restrict__ claims) {
     const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    const int row = pair / kQueryHeads;
-    const int head = pair % kQueryHeads;
+    const int row = pair / (kQueryHeads / 2);
+    const int head = 2 * (pair % (kQueryHeads / 2)) + (lane >> 4);
+    const int dim = 4 * (lane & 15);
     int cta_first = 0, cta_last = 0;
     if (row < batch) {
         if (row_pieces != nullptr) {
@@ -806,18 +810,19 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
     // The split kernel has completed: its slot claims are done with.
     if (claims != nullptr && blockIdx.x == 0 && threadIdx.x < kClaimWords) claims[threadIdx.x] = 0;
     if (row >= batch || cta_first == cta_last) return;  // written directly by the split kernel
-    float M = -INFINITY, L = 0.f, A0 = 0.f, A1 = 0.f;
+    float M = -INFINITY, L = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
     // Pieces in order, four at a time: all four partials are loaded before
     // any is merged, so a row costs about one L2 round trip per four pieces.
     constexpr int kBatch = 4;
     for (int c0 = cta_first; c0 <= cta_last; c0 += kBatch) {
-        float2 ml[kBatch], v[kBatch];
+        float2 ml[kBatch];
+        float4 v[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
             if (c0 + j <= cta_last) {
                 const int64_t idx = (static_cast<int64_t>(row) + c0 + j) * kQueryHeads + head;
                 ml[j] = *reinterpret_cast<const float2 *>(part_ml + idx * 2);
-                v[j] = *reinterpret_cast<const float2 *>(part_o + idx * kHeadDim + 2 * lane);
+                v[j] = *reinterpret_cast<const float4 *>(part_o + idx * kHeadDim + dim);
             }
         }
 #pragma unroll
@@ -825,13 +830,16 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
             if (c0 + j <= cta_last) {
                 const MergeWeights w = merge_weights(M, ml[j].x);
                 L = merge_value(L, ml[j].y, w);
-                A0 = merge_value(A0, v[j].x, w);
-                A1 = merge_value(A1, v[j].y, w);
+                A[0] = merge_value(A[0], v[j].x, w);
+                A[1] = merge_value(A[1], v[j].y, w);
+                A[2] = merge_value(A[2], v[j].z, w);
+                A[3] = merge_value(A[3], v[j].w, w);
             }
         }
     }
-    *reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + 2 * lane) =
-        __floats2half2_rn(__fdiv_rn(A0, L), __fdiv_rn(A1, L));
+    __half2 *dst = reinterpret_cast<__half2 *>(out + row * out_stride + head * kHeadDim + dim);
+    dst[0] = __floats2half2_rn(__fdiv_rn(A[0], L), __fdiv_rn(A[1], L));
+    dst[1] = __floats2half2_rn(__fdiv_rn(A[2], L), __fdiv_rn(A[3], L));
 }
 
 // ---------------------------------------------------------------------------
@@ -1106,7 +1114,7 @@ int launch_pass(int grid, const CUtensorMap &map, const LayerArgs &args, const i
     if (e != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string(what) + " launch failed: " + cudaGetErrorString(e));
     if (grid == 1) return PKV_OK;
     const int warps_per_cta = kCombineThreads / 32;
-    const int pairs = args.batch * kQueryHeads;
+    const int pairs = args.batch * (kQueryHeads / 2);
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3((pairs + warps_per_cta - 1) / warps_per_cta);
     config.blockDim = dim3(warps_per_cta * 32);
