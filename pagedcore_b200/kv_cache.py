@@ -257,6 +257,9 @@ class KVAllocator:
             raise ValueError("balance must be 'rows' or 'measured'")
         self._balance = balance
         self._speeds: dict[int, _SlotSpeeds] = {}
+        # Grid of every decode launch since the slot counters were last zeroed
+        # (None: launches outside a measured step, or of mixed grids).
+        self._window_grid: int | None = None
 
     # -- plumbing -------------------------------------------------------------
     @property
@@ -316,9 +319,7 @@ class KVAllocator:
         state = self._speeds.get(plan.grid)
         if state is None:
             state = self._speeds[plan.grid] = _SlotSpeeds(np.ones(plan.grid, dtype=np.float32))
-            counters = self._slot_counters(plan)
-            if counters is not None:
-                counters.zero_()  # the first measured step starts from zero
+            self._reset_slot_counters(plan.grid)  # the first measured step starts from zero
         if state.pending is not None and state.pending[1].query():
             counters = state.pending[0].numpy().astype(np.uint32).reshape(plan.grid, 4)
             seconds = counters.max(axis=1).astype(np.float64)
@@ -331,9 +332,27 @@ class KVAllocator:
                 state.updates += 1
         return state.weights
 
+    def _reset_slot_counters(self, grid: int) -> None:
+        """Zero every slot's counters: the next window holds launches of ``grid`` only."""
+        if self._workspace is not None:
+            start = kernels._CLAIM_BYTES // 4
+            self._workspace[start : start + 4 * kernels.decode_slots(self._pool.device)].zero_()
+        self._window_grid = grid
+
     def _measure_slots(self, plan: kernels.DecodePlan) -> None:
-        """After a staged step: copy out and clear its slot counters while calibrating."""
-        if self._balance != "measured" or plan.grid < 2:
+        """After a staged step: copy out and clear its slot counters while calibrating.
+
+        A measurement covers only steps of the plan's grid: launches of another
+        grid add to the same counters (a smaller grid's partials may even
+        overwrite them), so a step of another grid, or attention launched
+        outside a staged step, starts the window over.
+        """
+        if self._balance != "measured":
+            return
+        if self._window_grid != plan.grid:
+            self._reset_slot_counters(plan.grid)
+            return
+        if plan.grid < 2:
             return
         state = self._speeds.get(plan.grid)
         counters = self._slot_counters(plan)
@@ -815,6 +834,7 @@ class KVAllocator:
     def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
         """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""
         self._check_worker()
+        self._window_grid = None  # this launch adds to the slot counters outside a measured window
         if out is None:
             out = torch.empty(query.shape, dtype=torch.float16, device=self._pool.device)
         kernels.decode_attention(

@@ -57,14 +57,14 @@ class StressRun:
     """The config 5 workload on one device, driven through ``Worker``."""
 
     def __init__(self, device: torch.device, seed: int = 5, rows: int = ROWS, context: int = CONTEXT,
-                 new_prompt: int = NEW_PROMPT) -> None:
+                 new_prompt: int = NEW_PROMPT, balance: str = "rows") -> None:
         self.device = device
         self.rng = workloads.rng(seed, 50)
         self.context = context
         self.new_prompt = new_prompt
         blocks = int(POOL_SHARE * rows * (context // 16))
         pool = torch.empty((LAYERS, 2, blocks, 16, 4, 64), dtype=torch.float16, device=device)
-        self.allocator = KVAllocator(pool, validation="incremental", balance="rows")
+        self.allocator = KVAllocator(pool, validation="incremental", balance=balance)
         generator = torch.Generator(device=device).manual_seed(seed)
         self.kv = torch.randn(LAYERS, context, 4, 64, dtype=torch.float16, device=device, generator=generator)
         self.q = torch.randn(LAYERS, rows, 32, 64, dtype=torch.float16, device=device, generator=generator)
