@@ -214,6 +214,7 @@ class _SlotSpeeds:
 
 
 _SPEED_UPDATES = 6  # weight updates before the weights freeze
+_PIECES_PER_ROW_MAX = 8  # steps with more pieces per row than this are not measured
 
 
 class KVAllocator:
@@ -339,15 +340,21 @@ class KVAllocator:
             self._workspace[start : start + 4 * kernels.decode_slots(self._pool.device)].zero_()
         self._window_grid = grid
 
-    def _measure_slots(self, plan: kernels.DecodePlan) -> None:
-        """After a staged step: copy out and clear its slot counters while calibrating.
+    def _measure_slots(self, plan: kernels.DecodePlan, rows: int) -> None:
+        """After a staged step of ``rows`` rows: copy out and clear its slot counters while calibrating.
 
         A measurement covers only steps of the plan's grid: launches of another
         grid add to the same counters (a smaller grid's partials may even
         overwrite them), so a step of another grid, or attention launched
-        outside a staged step, starts the window over.
+        outside a staged step, starts the window over.  Steps with fewer than
+        one row per _PIECES_PER_ROW_MAX pieces are not measured: there each
+        row spans many pieces and a slot's time reflects where the row
+        boundaries fall in this batch more than its SM's speed.
         """
         if self._balance != "measured":
+            return
+        if rows * _PIECES_PER_ROW_MAX < plan.grid:
+            self._window_grid = None
             return
         if self._window_grid != plan.grid:
             self._reset_slot_counters(plan.grid)
@@ -539,7 +546,7 @@ class KVAllocator:
             raise
         else:
             self._ledger.decode_commit()
-            self._measure_slots(plan)
+            self._measure_slots(plan, count)
         finally:
             self._staged = None
             self._uploads.release(upload)

@@ -57,7 +57,7 @@ class StressRun:
     """The config 5 workload on one device, driven through ``Worker``."""
 
     def __init__(self, device: torch.device, seed: int = 5, rows: int = ROWS, context: int = CONTEXT,
-                 new_prompt: int = NEW_PROMPT, balance: str = "rows") -> None:
+                 new_prompt: int = NEW_PROMPT, balance: str = "measured") -> None:
         self.device = device
         self.rng = workloads.rng(seed, 50)
         self.context = context
