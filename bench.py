@@ -648,6 +648,208 @@ def run_stress_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def run_append_arm(args: argparse.Namespace) -> None:
+    """BASELINE config 2(a): prompt K/V appends with fused K-RoPE after allocator churn.
+
+    A 4096-block pool fragmented by the seeded 10k-op churn, then 8 prompts of
+    U[1, 2047] tokens.  `value` times the append kernel (`pkv_append_kv`, K
+    rotated at its positions, K and V scattered through the prompt's slots)
+    over the 8 prompts with K/V resident in HBM; `e2e` times the public
+    `KVAllocator.append(..., rotate=True)` with every prompt's K/V copied in
+    from pinned host memory, the requests released and re-created around it,
+    and the device error flag read back per step.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from pagedcore_b200 import kernels, workloads
+    from pagedcore_b200.engine_types import KVReservation, RequestId
+    from pagedcore_b200.kv_cache import KVAllocator
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    host_affinity = _bind_host_cores(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    seed = 2 + 1000 * rank
+    case = workloads.append_case(seed=seed)
+    pool = torch.empty((LAYERS, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
+    allocator = KVAllocator(pool, validation="incremental")
+    fill = torch.zeros(LAYERS, 128, 4, 64, dtype=torch.float16, device=device)  # churn data is irrelevant
+    for op in case.churn:
+        request = RequestId(f"churn{op.request}")
+        if op.kind == "create":
+            allocator.create(KVReservation(request, op.credits))
+            allocator.append(request, fill[:, : op.tokens], fill[:, : op.tokens])
+        else:
+            allocator.release_all(request)
+    prompts = []
+    for prompt in case.prompts:
+        request = RequestId(f"prompt{prompt.request}")
+        key_host = torch.from_numpy(prompt.key).pin_memory()
+        value_host = torch.from_numpy(prompt.value).pin_memory()
+        key, value = key_host.to(device), value_host.to(device)
+        allocator.create(KVReservation(request, prompt.credits))
+        allocator.append(request, key, value, rotate=True)
+        tokens = key.shape[1]
+        table = np.asarray(allocator.block_table(request), dtype=np.int64)
+        positions = np.arange(tokens, dtype=np.int32)
+        slots = (table[positions // 16] * 16 + positions % 16).astype(np.int32)
+        prompts.append((request, prompt.credits, key, value, key_host, value_host,
+                        torch.from_numpy(slots).to(device), torch.from_numpy(positions).to(device)))
+    total_tokens = sum(p[2].shape[1] for p in prompts)
+    # Algorithmic bytes: per (layer, token) K and V read and written (4 x 512 B);
+    # per token its slot and position and one RoPE row (32 cos + 32 sin FP16).
+    step_bytes = total_tokens * (LAYERS * 4 * 512 + 8 + 128)
+    stream = torch.cuda.current_stream(device)
+
+    def kernel_step() -> None:
+        for _, _, key, value, _, _, slots, positions in prompts:
+            kernels.append_kv(pool, key, value, slots, layer_begin=0, error_flag=allocator._error,
+                              positions=positions, rope_table=allocator._rope)
+
+    for _ in range(args.warmup):
+        kernel_step()
+    torch.cuda.synchronize(device)
+    # The step's launches replay as one CUDA graph: each kernels.append_kv
+    # call costs 15-20 us of Python and ctypes on the host, more than most of
+    # these launches take on the GPU, and `value` is the device's throughput.
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        kernel_step()
+    stream.wait_stream(side)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    kernel_ms = start.elapsed_time(end) / args.steps
+    allocator.check_device_errors()
+
+    # End to end through the public API, K/V from pinned host memory.
+    staging = [(torch.empty_like(p[2]), torch.empty_like(p[3])) for p in prompts]
+
+    def public_step() -> None:
+        for request, _, _, _, _, _, _, _ in prompts:
+            allocator.release_all(request)
+        for (request, credits, _, _, key_host, value_host, _, _), (key, value) in zip(prompts, staging):
+            allocator.create(KVReservation(request, credits))
+            key.copy_(key_host, non_blocking=True)
+            value.copy_(value_host, non_blocking=True)
+            allocator.append(request, key, value, rotate=True)
+        allocator.check_device_errors()  # the step's device-to-host read
+
+    for _ in range(args.warmup):
+        public_step()
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(args.steps):
+        public_step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = start.elapsed_time(end) / args.steps
+
+    times = torch.tensor([kernel_ms, e2e_ms], dtype=torch.float64, device=device)
+    counts = torch.tensor([total_tokens], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM)
+    kernel_ms, e2e_ms = times.tolist()
+    all_tokens = counts.item()
+    if rank == 0:
+        peak, peak_kind = _peak_hbm()
+        achieved = step_bytes / (kernel_ms / 1000.0) / 1e9
+        line = {
+            "metric": "prompt KV append tokens/s with fused K-RoPE (BASELINE config 2a)",
+            "value": all_tokens / (kernel_ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": kernel_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded K/V ~N(0,1), prompt lengths U[1, 2047]); the reference publishes no inputs",
+            "config": {
+                "workload": f"config 2a per GPU: pool of {case.num_blocks} blocks after a seeded "
+                            f"{len(case.churn)}-op alloc/free churn, {len(prompts)} prompts ({total_tokens} tokens "
+                            "on rank 0) appended with K rotated at positions 0..T-1; one step = all prompts",
+                "l2": f"inputs larger than L2: each step reads {2 * LAYERS * total_tokens * 512 / 1e6:.0f} MB of "
+                      "K/V (L2 is 126 MB)",
+                "parallelism": f"dp{world} (independent prompts, one KV pool per GPU, no collective)",
+                "launch": "the step's 8 append launches replayed as one CUDA graph (value); e2e makes the "
+                          "public calls",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "append_kv_kernel (K-RoPE + K/V scatter through slot ids)",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "algorithmic_bytes_per_step": step_bytes,
+                "avg_launch_ms": kernel_ms / len(prompts),
+                "traffic": None,
+            },
+            "e2e": {
+                "value": all_tokens / (e2e_ms / 1000.0),
+                "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * LAYERS * total_tokens * 512 + 8 * total_tokens,
+                "d2h_bytes_per_step": 4,
+                "path": "KVAllocator.release_all + create + append(rotate=True) per prompt, K/V copied from pinned "
+                        "host memory each step, error flag read back per step",
+            },
+            "gpu_launches": args.steps * len(prompts),
+            "clocks": clocks.summary(),
+            "host_affinity": host_affinity,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import kv_write, rope
+
+            table = rope.cos_sin_table()
+            host_pool = np.zeros((LAYERS, 2, case.num_blocks, 16, 4, 64), dtype=np.float16)
+            sample = case.prompts[:2]
+            begin = time.perf_counter()
+            repeats = 0
+            while time.perf_counter() - begin < 10.0:
+                for prompt, entry in zip(sample, prompts):
+                    tokens = prompt.key.shape[1]
+                    kv_write.append_rotated(host_pool, prompt.key, prompt.value, entry[6].cpu().numpy(),
+                                            np.arange(tokens, dtype=np.int32), table)
+                repeats += 1
+            seconds = time.perf_counter() - begin
+            sample_tokens = sum(p.key.shape[1] for p in sample)
+            line["cpu_baseline"] = {
+                "value": repeats * sample_tokens / seconds,
+                "unit": "tokens/s",
+                "cores": 1,
+                "kind": "port",
+                "sample": f"the first 2 prompts ({sample_tokens} tokens) appended {repeats} times, one thread, "
+                          f"oracle restatement of apply_rope + the pool copy ({seconds:.1f}s)",
+            }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -657,8 +859,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
-    parser.add_argument("--workload", choices=("decode", "stress"), default="decode",
-                        help="decode: config 4 (the headline line); stress: config 5 (allocator churn)")
+    parser.add_argument("--workload", choices=("decode", "stress", "append"), default="decode",
+                        help="decode: config 4 (the headline line); stress: config 5 (allocator churn); "
+                             "append: config 2a (prompt K/V appends)")
     parser.add_argument("--stress-iterations", type=int, default=300)
     parser.add_argument("--stress-warmup", type=int, default=200)
     args = parser.parse_args()
@@ -669,6 +872,8 @@ def main() -> None:
         run_reference_arm(args)
     elif args.workload == "stress":
         run_stress_arm(args)
+    elif args.workload == "append":
+        run_append_arm(args)
     else:
         run_gpu_arm(args)
 
