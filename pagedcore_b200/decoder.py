@@ -23,7 +23,7 @@ the batch, so its rows may differ from ``decode_paged`` in the last bits.
 
 from __future__ import annotations
 
-from collections.abc import Sequence
+from collections.abc import Callable, Sequence
 
 import torch
 import torch.nn.functional as F
@@ -182,26 +182,36 @@ class BatchedDecoder:
         self.qkv = [torch.cat((layer.q_proj, layer.k_proj, layer.v_proj)) for layer in weights.layers]
         self.gate_up = [torch.cat((layer.gate_proj, layer.up_proj)) for layer in weights.layers]
 
+    def forward(self, input_ids: Tensor, attend: Callable[[int, Tensor, Tensor, Tensor], Tensor]) -> Tensor:
+        """The decoder stack for token ids [B, 1]; ``attend(layer, q, k, v)`` is the decode layer.
+
+        q [B, 32, 64], k and v [B, 4, 64] are unrotated views of the layer's
+        fused Q/K/V projection (rows 2560 elements apart); ``attend`` returns
+        the FP16 attention [B, 32, 64].  Shared by ``step`` and the CUDA-graph
+        form (``graph.DecoderStepGraph``), so both run the same op sequence.
+        """
+        weights = self.weights
+        batch = input_ids.shape[0]
+        q_width, kv_width = QUERY_HEADS * HEAD_DIM, KV_HEADS * HEAD_DIM
+        hidden = F.embedding(input_ids, weights.embedding)  # [B, 1, 2048]
+        for index, layer in enumerate(weights.layers):
+            qkv = F.linear(rms_norm(hidden, layer.input_norm), self.qkv[index]).view(batch, -1)
+            query = qkv[:, :q_width].view(batch, QUERY_HEADS, HEAD_DIM)
+            key = qkv[:, q_width : q_width + kv_width].view(batch, KV_HEADS, HEAD_DIM)
+            value = qkv[:, q_width + kv_width :].view(batch, KV_HEADS, HEAD_DIM)
+            # RoPE(Q, K) + new-token KV write + attention: one fused launch.
+            attention = attend(index, query, key, value)
+            hidden = hidden + F.linear(attention.view(batch, 1, HIDDEN), layer.o_proj)
+            gate, up = F.linear(rms_norm(hidden, layer.post_attention_norm), self.gate_up[index]).chunk(2, -1)
+            hidden = hidden + F.linear(F.silu(gate) * up, layer.down_proj)
+        return final_logits(hidden, weights)
+
     @torch.inference_mode()
     def step(self, input_ids: Tensor, allocator: KVAllocator, request_ids: tuple[RequestId, ...]) -> Tensor:
         """One token for every request; returns logits [B, 1, V] in request order."""
-        weights = self.weights
-        _check_decode(input_ids, weights, request_ids)
-        batch = len(request_ids)
-        q_width, kv_width = QUERY_HEADS * HEAD_DIM, KV_HEADS * HEAD_DIM
+        _check_decode(input_ids, self.weights, request_ids)
         with allocator.append_decode(request_ids):
-            hidden = F.embedding(input_ids, weights.embedding)  # [B, 1, 2048]
-            for index, layer in enumerate(weights.layers):
-                qkv = F.linear(rms_norm(hidden, layer.input_norm), self.qkv[index]).view(batch, -1)
-                query = qkv[:, :q_width].view(batch, QUERY_HEADS, HEAD_DIM)
-                key = qkv[:, q_width : q_width + kv_width].view(batch, KV_HEADS, HEAD_DIM)
-                value = qkv[:, q_width + kv_width :].view(batch, KV_HEADS, HEAD_DIM)
-                # RoPE(Q, K) + new-token KV write + attention: one fused launch.
-                attention = allocator.decode_layer(index, query, key, value)
-                hidden = hidden + F.linear(attention.view(batch, 1, HIDDEN), layer.o_proj)
-                gate, up = F.linear(rms_norm(hidden, layer.post_attention_norm), self.gate_up[index]).chunk(2, -1)
-                hidden = hidden + F.linear(F.silu(gate) * up, layer.down_proj)
-            return final_logits(hidden, weights)
+            return self.forward(input_ids, allocator.decode_layer)
 
 
 def decode_batched(

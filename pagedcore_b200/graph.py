@@ -131,3 +131,94 @@ class DecodeStepGraph:
             ledger.decode_mark_layers(0, _LAYERS)
             staged.written = _LAYERS
         return out
+
+
+class DecoderStepGraph:
+    """``BatchedDecoder`` steps of up to ``rows`` requests replayed as CUDA graphs.
+
+    A decoder step launches about a dozen kernels per layer (norms, the fused
+    Q/K/V and gate/up GEMMs, the decode layer, the output and down
+    projections, residual adds) plus the embedding and the logits: over 300
+    launches whose Python and launch costs exceed the GPU time at small
+    batches.  Here the whole step, ``BatchedDecoder.forward`` with the fused
+    decode layer launched on the step's padded tables, is captured once per
+    upload buffer and replayed: the host stages the step (ledger, tables, one
+    upload), copies the token ids into a fixed buffer and launches the graph.
+    ``step(input_ids, request_ids)`` returns the logits [B, 1, V] of
+    ``BatchedDecoder.step`` for the same inputs (the GEMMs run over all
+    ``rows`` rows, so their rounding may differ in the last bits).
+    """
+
+    def __init__(self, decoder, allocator: KVAllocator, *, rows: int, max_graphs: int = 4) -> None:
+        if rows < 1:
+            raise ValueError("a decoder step graph needs at least one row")
+        self.decoder = decoder
+        self.allocator = allocator
+        self.rows = rows
+        device = allocator.pool.device
+        self.grid = kernels.decode_slots(device)
+        self.max_graphs = max_graphs
+        with torch.inference_mode(False):  # fixed buffers, updated in place in any mode
+            self.ids = torch.zeros((rows, 1), dtype=torch.int64, device=device)
+            self.attention = torch.empty((rows, 32, 64), dtype=torch.float16, device=device)
+        self._graphs: dict[tuple, tuple[torch.cuda.CUDAGraph, Tensor]] = {}
+        self.captures = 0
+
+    def _capture(self, args: tuple) -> tuple[torch.cuda.CUDAGraph, Tensor]:
+        allocator = self.allocator
+        (pool, num_blocks, rope, lengths, prefix, flat, pieces, row_pieces, bound, grid, per_cta, big, tail, ws,
+         ws_bytes, err) = args
+        side = torch.cuda.Stream(allocator.pool.device)
+        side.wait_stream(allocator._stream)
+        out = self.attention
+
+        def attend(layer: int, q: Tensor, k: Tensor, v: Tensor) -> Tensor:
+            # The previous kernel is a GEMM of this step, not a decode combine:
+            # no early K/V (it would only save the launch, which a GEMM
+            # predecessor does not overlap).
+            check(
+                lib.pkv_decode_layer(
+                    pool, num_blocks, layer, q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0),
+                    rope, lengths, prefix, flat, pieces, row_pieces, self.rows, bound, grid, per_cta, big, tail,
+                    out.data_ptr(), out.stride(0), ws, ws_bytes, err, 0, side.cuda_stream,
+                )
+            )
+            return out
+
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            logits = self.decoder.forward(self.ids, attend)
+        allocator._stream.wait_stream(side)
+        self.captures += 1
+        return graph, logits
+
+    @torch.inference_mode()
+    def step(self, input_ids: Tensor, request_ids: Sequence[RequestId]) -> Tensor:
+        allocator = self.allocator
+        requests = tuple(request_ids)
+        count = len(requests)
+        if not 1 <= count <= self.rows:
+            raise ValueError(f"a decoder step graph serves 1 to {self.rows} requests, not {count}")
+        if (
+            input_ids.dtype != torch.int64
+            or input_ids.shape != (count, 1)
+            or input_ids.device != allocator.pool.device
+        ):
+            raise ValueError("input_ids must be int64 [batch, 1] matching request IDs on the pool device")
+        with allocator.append_decode(requests, layout=(self.rows, self.grid)):
+            staged = allocator._staged
+            fixed = allocator._decode_layer_args(staged.staged_batch, self.rows, self.grid)
+            args = (*fixed[:8], staged.flat_capacity, self.grid, 1, self.grid, 1, *fixed[13:16])
+            entry = self._graphs.get(args)
+            if entry is None:
+                if len(self._graphs) >= self.max_graphs:
+                    self._graphs.clear()
+                entry = self._graphs[args] = self._capture(args)
+            graph, logits = entry
+            self.ids[:count].copy_(input_ids)
+            ledger = allocator._ledger
+            ledger.decode_check(-1, 0)  # a fresh staged step: layer 0 is next
+            graph.replay()
+            ledger.decode_mark_layers(0, _LAYERS)
+            staged.written = _LAYERS
+            return logits[:count].clone()

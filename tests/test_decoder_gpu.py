@@ -22,6 +22,7 @@ import torch
 from pagedcore_b200 import decoder
 from pagedcore_b200.decoder import BatchedDecoder, decode_paged, prefill, prefill_paged
 from pagedcore_b200.engine_types import CapacityCounts, KVReservation, RequestId
+from pagedcore_b200.graph import DecoderStepGraph
 from pagedcore_b200.kv_cache import KVAllocator
 from pagedcore_b200.weights import random_weights
 from tests.conftest import ROOT, cuda_device
@@ -148,6 +149,33 @@ def test_batched_decoder_matches_decode_paged(small) -> None:
     fused.check_device_errors()
 
 
+def test_decoder_step_graph_matches_the_batched_decoder(small) -> None:
+    """One captured graph per upload buffer serves batches of every size and order."""
+    device = cuda_device()
+    graphed, requests = prefilled(small, SMALL_ROWS, device, extra=12)
+    eager, _ = prefilled(small, SMALL_ROWS, device, extra=12)
+    engine = BatchedDecoder(small)
+    steps = DecoderStepGraph(engine, graphed, rows=len(requests))
+    for step, rows in enumerate(((0, 1, 2), (2, 0), (1,), (0, 1, 2), (1, 2), (2, 1, 0))):
+        chosen = tuple(requests[row] for row in rows)
+        tokens = torch.tensor([[3 + row + step] for row in rows], device=device)
+        expected = engine.step(tokens, eager, chosen)
+        actual = steps.step(tokens, chosen)
+        torch.testing.assert_close(actual, expected, atol=LOGIT_TOL, rtol=LOGIT_TOL)
+        assert torch.equal(actual.argmax(-1), expected.argmax(-1))
+    assert steps.captures == 2  # one per upload buffer
+    assert graphed.capacity() == eager.capacity()
+    for request in requests:
+        assert graphed.cached_length(request) == eager.cached_length(request)
+        for block in range(len(graphed.block_table(request))):
+            for a, b in zip(graphed.read_block(request, block), eager.read_block(request, block), strict=True):
+                torch.testing.assert_close(a, b, atol=2e-3, rtol=2e-3)
+    with pytest.raises(ValueError, match="serves 1 to 3"):
+        steps.step(torch.zeros((4, 1), dtype=torch.int64, device=device), requests + requests[:1])
+    assert graphed.capacity() == eager.capacity()
+    graphed.check_device_errors()
+
+
 @pytest.mark.parametrize("fault", ["attention", "logits"])
 def test_a_failed_decode_leaves_every_row_unchanged_and_can_be_retried(small, fault, monkeypatch) -> None:
     device = cuda_device()
@@ -220,7 +248,7 @@ def _teacher_forced(record, step_fn) -> tuple[float, int, list[int]]:
     return worst, agree, disagree
 
 
-@pytest.mark.parametrize("path", ["per_row", "batched", "paged_prefill"])
+@pytest.mark.parametrize("path", ["per_row", "batched", "graphed", "paged_prefill"])
 def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
     record, weights = cfg3
     device = cuda_device()
@@ -233,6 +261,7 @@ def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
     else:
         prompt_logits = prefill_paged(prompt, weights, allocator, request)[0, -1]
     engine = BatchedDecoder(weights)
+    graph = DecoderStepGraph(engine, allocator, rows=1)
     ids = record["greedy_ids"]
 
     def step_fn(step: int) -> torch.Tensor:
@@ -241,6 +270,8 @@ def test_config3_greedy_decode_follows_the_reference(cfg3, path) -> None:
         token = torch.tensor([[ids[step - 1]]], dtype=torch.int64, device=device)
         if path == "per_row":
             return decode_paged(token, weights, allocator, (request,))[0, 0]
+        if path == "graphed":
+            return graph.step(token, (request,))[0, 0]
         return engine.step(token, allocator, (request,))[0, 0]
 
     worst, agree, disagree = _teacher_forced(record, step_fn)
