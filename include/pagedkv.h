@@ -271,8 +271,9 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
  * call on a device looks up the array's device address (cudaGetSymbolAddress)
  * and sets the kernel attributes with that device current; make that first
  * call before any stream capture.  All calls share the array and it keeps the
- * last call's contents (nothing in it needs to start at zero: every partial
- * is written before it is read within one call), so calls that overlap on the
+ * last call's contents (every partial is written before it is read within one
+ * call; the slot-claim counters in it start at zero when the library loads
+ * and every call leaves them at zero), so calls that overlap on the
  * GPU - on different streams, or on one device from different threads - race
  * and must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
 int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
@@ -281,6 +282,25 @@ int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t l
                                  int32_t total_blocks, int32_t grid, int32_t blocks_per_cta, int32_t big_ctas,
                                  int32_t tail_blocks, void *out, int64_t out_stride, int32_t *error_flag,
                                  void *stream);
+
+/* ---- Batched decoder step: fused elementwise chains ------------------------
+ * Replace chains of eager ops of the reference's dense decoder
+ * (src/pagedcore/dense.py) for the rows of a batched decode step; each keeps
+ * the chain's FP16 rounding points (only the order of the FP32 sum of squares
+ * differs).  FP16 row-major tensors, 16-byte aligned; kernels on `stream`. */
+
+/* Residual add and RMSNorm (dense.py:17-21): when delta is not null,
+ * hidden[r] = fp16(hidden[r] + delta[r]) in place; then
+ * out[r] = fp16(weight * fp16(hidden[r] * rsqrt(mean(hidden[r]^2) + eps))),
+ * the mean and rsqrt in FP32.  hidden, delta, out [rows][dim], weight [dim];
+ * dim a multiple of 8 up to 8192. */
+int pkv_add_rms_norm(void *hidden, const void *delta, const void *weight, void *out, int32_t rows, int32_t dim,
+                     float eps, void *stream);
+
+/* SwiGLU's product (dense.py:84-91): out[r][c] = fp16(fp16(silu(g)) * u) with
+ * g = gate_up[r][c], u = gate_up[r][inter + c], silu in FP32.  gate_up
+ * [rows][2 * inter], out [rows][inter]. */
+int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, void *stream);
 
 #ifdef __cplusplus
 }

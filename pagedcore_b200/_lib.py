@@ -8,7 +8,7 @@ operation of this package goes through it and there is no fallback path.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_int, c_int32, c_int64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_void_p
 from pathlib import Path
 
 from pagedcore_b200 import build as _build
@@ -66,6 +66,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_ledger_debug_set_table": (c_int, [c_void_p, c_int64, i32p, c_int32, c_int32]),
     "pkv_ledger_debug_set_free": (c_int, [c_void_p, i32p, c_int32]),
     "pkv_rope_table_bytes": (c_int64, []),
+    "pkv_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
+    "pkv_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     "pkv_append_kv": (
         c_int,
         [

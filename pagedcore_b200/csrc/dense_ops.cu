@@ -1,0 +1,155 @@
+// Fused elementwise steps of the batched TinyLlama decoder step.
+//
+// The reference's decoder (src/pagedcore/dense.py) runs each of these as a
+// chain of eager FP16/FP32 tensor ops; on a batch of decode rows every op is
+// a separate launch over a few KB, so a decoder step was mostly launch
+// latency.  Each kernel here does one chain in one pass and keeps the
+// chain's rounding points:
+//
+//   add_rms_norm  (dense.py:17-21, and the residual adds of dense.py /
+//                  decoder.py that precede each norm)
+//       hidden = fp16(hidden + delta)                      (when delta given)
+//       y      = fp16(hidden * rsqrt(mean(hidden^2) + eps))   in FP32
+//       out    = fp16(weight * y)
+//   silu_mul      (dense.py:84-91)
+//       out = fp16(fp16(silu(gate)) * up),  silu(x) = x / (1 + exp(-x)) in FP32
+//
+// Every elementwise step is the FP32 operation on FP16 operands rounded to
+// FP16, which is what the eager ops compute.  The one difference is the
+// order of the FP32 sum of squares (a tree over the row here), so a norm can
+// differ from the eager one in the last bit of rare elements.
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "pagedkv.h"
+#include "status.h"
+
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kChunk = 8;  // FP16 values per 16-byte access
+
+__device__ __forceinline__ float h2f(__half x) { return __half2float(x); }
+
+// One CTA per row of `dim` values (dim a multiple of 8, at most
+// kNormThreads * kChunk * kMaxChunksPerThread).
+constexpr int kMaxChunksPerThread = 4;
+
+__global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(
+    __half *__restrict__ hidden, const __half *__restrict__ delta, const __half *__restrict__ weight,
+    __half *__restrict__ out, int dim, float eps) {
+    __shared__ float partial[kNormThreads / 32];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * dim;
+    const int chunks = dim / kChunk;
+    float v[kMaxChunksPerThread][kChunk];
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxChunksPerThread; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < chunks) {
+            uint4 raw = *reinterpret_cast<const uint4 *>(hidden + base + c * kChunk);
+            const __half *h = reinterpret_cast<const __half *>(&raw);
+            if (delta != nullptr) {
+                const uint4 draw = *reinterpret_cast<const uint4 *>(delta + base + c * kChunk);
+                const __half *d = reinterpret_cast<const __half *>(&draw);
+                uint4 sum_raw;
+                __half *s = reinterpret_cast<__half *>(&sum_raw);
+#pragma unroll
+                for (int i = 0; i < kChunk; ++i) s[i] = __float2half_rn(h2f(h[i]) + h2f(d[i]));
+                *reinterpret_cast<uint4 *>(hidden + base + c * kChunk) = sum_raw;
+                raw = sum_raw;
+                h = reinterpret_cast<const __half *>(&raw);
+            }
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                v[j][i] = h2f(h[i]);
+                sum += v[j][i] * v[j][i];
+            }
+        }
+    }
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, offset);
+    if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) total += partial[w];
+    const float inv = rsqrtf(total / static_cast<float>(dim) + eps);
+#pragma unroll
+    for (int j = 0; j < kMaxChunksPerThread; ++j) {
+        const int c = threadIdx.x + j * kNormThreads;
+        if (c < chunks) {
+            const uint4 wraw = *reinterpret_cast<const uint4 *>(weight + c * kChunk);
+            const __half *w = reinterpret_cast<const __half *>(&wraw);
+            uint4 oraw;
+            __half *o = reinterpret_cast<__half *>(&oraw);
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                const __half y = __float2half_rn(v[j][i] * inv);
+                o[i] = __float2half_rn(h2f(w[i]) * h2f(y));
+            }
+            *reinterpret_cast<uint4 *>(out + base + c * kChunk) = oraw;
+        }
+    }
+}
+
+// gate_up [rows][2 * inter] (gate, then up) -> out [rows][inter].
+__global__ void silu_mul_kernel(const __half *__restrict__ gate_up, __half *__restrict__ out, int64_t rows,
+                                int inter) {
+    const int64_t total = rows * inter;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += step) {
+        const int64_t row = e / inter;
+        const int col = static_cast<int>(e - row * inter);
+        const float g = h2f(gate_up[row * 2 * inter + col]);
+        const __half silu = __float2half_rn(g / (1.0f + expf(-g)));
+        const __half up = gate_up[row * 2 * inter + inter + col];
+        out[e] = __float2half_rn(h2f(silu) * h2f(up));
+    }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int pkv_add_rms_norm(void *hidden, const void *delta, const void *weight, void *out, int32_t rows,
+                                int32_t dim, float eps, void *stream) {
+    pkv::clear_error();
+    if (hidden == nullptr || weight == nullptr || out == nullptr) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: hidden, weight and out are required");
+    }
+    if (rows < 0 || dim < kChunk || dim % kChunk || dim > kNormThreads * kChunk * kMaxChunksPerThread) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: dim must be a multiple of 8 up to 8192");
+    }
+    if (!aligned16(hidden) || !aligned16(weight) || !aligned16(out) || (delta && !aligned16(delta))) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: tensors must be 16-byte aligned");
+    }
+    if (rows == 0) return PKV_OK;
+    add_rms_norm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__half *>(hidden), static_cast<const __half *>(delta), static_cast<const __half *>(weight),
+        static_cast<__half *>(out), dim, eps);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("rms norm launch failed: ") + cudaGetErrorString(err));
+    return PKV_OK;
+}
+
+extern "C" int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, void *stream) {
+    pkv::clear_error();
+    if (gate_up == nullptr || out == nullptr || rows < 0 || inter < 1) {
+        return pkv::fail(PKV_VALUE_ERROR, "silu_mul: bad arguments");
+    }
+    if (rows == 0) return PKV_OK;
+    const int64_t total = static_cast<int64_t>(rows) * inter;
+    const int threads = 256;
+    const int64_t wanted = (total + threads - 1) / threads;
+    const int grid = static_cast<int>(wanted < 4096 ? wanted : 4096);
+    silu_mul_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half *>(gate_up), static_cast<__half *>(out), rows, inter);
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(err));
+    return PKV_OK;
+}

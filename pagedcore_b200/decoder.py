@@ -16,9 +16,11 @@ Drop-in for the paged half of PagedCore's decoder.py:
   rest of the batch, bit for bit.
 
 ``BatchedDecoder`` is the throughput form: per layer one Q/K/V GEMM and one
-gate/up GEMM over the whole batch, and the fused decode-layer launch
-(Q/K RoPE, new-token KV write and attention in one kernel).  Its GEMMs see
-the batch, so its rows may differ from ``decode_paged`` in the last bits.
+gate/up GEMM over the whole batch, the fused decode-layer launch (Q/K RoPE,
+new-token KV write and attention in one kernel), and fused residual-add +
+RMSNorm and SwiGLU-product kernels in place of their eager op chains.  Its
+GEMMs see the batch and its norms sum in another order, so its rows may
+differ from ``decode_paged`` in the last bits.
 """
 
 from __future__ import annotations
@@ -29,6 +31,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
+from pagedcore_b200 import kernels
 from pagedcore_b200.attention import paged_attention
 from pagedcore_b200.dense import (
     apply_rope,
@@ -189,22 +192,30 @@ class BatchedDecoder:
         fused Q/K/V projection (rows 2560 elements apart); ``attend`` returns
         the FP16 attention [B, 32, 64].  Shared by ``step`` and the CUDA-graph
         form (``graph.DecoderStepGraph``), so both run the same op sequence.
+        The residual stream is one FP16 [B, 2048] buffer; each RMSNorm takes
+        the residual add before it in the same kernel (``kernels.add_rms_norm``)
+        and SwiGLU's product is one kernel (``kernels.silu_mul``), with the
+        rounding points of the reference's eager ops (dense.py:17-21, 84-91).
         """
         weights = self.weights
         batch = input_ids.shape[0]
         q_width, kv_width = QUERY_HEADS * HEAD_DIM, KV_HEADS * HEAD_DIM
-        hidden = F.embedding(input_ids, weights.embedding)  # [B, 1, 2048]
+        hidden = F.embedding(input_ids, weights.embedding).view(batch, HIDDEN)  # updated in place
+        x = torch.empty_like(hidden)
+        delta = None  # the output still to be added to the residual stream
         for index, layer in enumerate(weights.layers):
-            qkv = F.linear(rms_norm(hidden, layer.input_norm), self.qkv[index]).view(batch, -1)
+            kernels.add_rms_norm(hidden, delta, layer.input_norm, x)
+            qkv = F.linear(x, self.qkv[index])
             query = qkv[:, :q_width].view(batch, QUERY_HEADS, HEAD_DIM)
             key = qkv[:, q_width : q_width + kv_width].view(batch, KV_HEADS, HEAD_DIM)
             value = qkv[:, q_width + kv_width :].view(batch, KV_HEADS, HEAD_DIM)
             # RoPE(Q, K) + new-token KV write + attention: one fused launch.
             attention = attend(index, query, key, value)
-            hidden = hidden + F.linear(attention.view(batch, 1, HIDDEN), layer.o_proj)
-            gate, up = F.linear(rms_norm(hidden, layer.post_attention_norm), self.gate_up[index]).chunk(2, -1)
-            hidden = hidden + F.linear(F.silu(gate) * up, layer.down_proj)
-        return final_logits(hidden, weights)
+            delta = F.linear(attention.view(batch, HIDDEN), layer.o_proj)
+            kernels.add_rms_norm(hidden, delta, layer.post_attention_norm, x)
+            delta = F.linear(kernels.silu_mul(F.linear(x, self.gate_up[index])), layer.down_proj)
+        kernels.add_rms_norm(hidden, delta, weights.final_norm, x)
+        return F.linear(x, weights.lm_head).view(batch, 1, -1)
 
     @torch.inference_mode()
     def step(self, input_ids: Tensor, allocator: KVAllocator, request_ids: tuple[RequestId, ...]) -> Tensor:

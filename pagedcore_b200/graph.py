@@ -185,6 +185,11 @@ class DecoderStepGraph:
             )
             return out
 
+        # One forward outside the capture first, with an attention stand-in
+        # that touches no pool data: cuBLAS creates its handle and workspace
+        # on first use on a stream, which must not happen while capturing.
+        with torch.cuda.stream(side):
+            self.decoder.forward(self.ids, lambda layer, q, k, v: out)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side):
             logits = self.decoder.forward(self.ids, attend)

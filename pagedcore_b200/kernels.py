@@ -336,3 +336,33 @@ def decode_layer(
         )
     )
     return out
+
+
+def add_rms_norm(hidden: Tensor, delta: Tensor | None, weight: Tensor, out: Tensor, eps: float = 1e-5) -> Tensor:
+    """``hidden += delta`` (FP16, in place, when given), then ``out = rms_norm(hidden) * weight``.
+
+    hidden, delta, out FP16 [rows, dim] contiguous; weight FP16 [dim].  Same
+    rounding points as dense.rms_norm after an FP16 residual add.
+    """
+    rows, dim = hidden.shape
+    for name, tensor, shape in (("hidden", hidden, (rows, dim)), ("out", out, (rows, dim)),
+                                ("weight", weight, (dim,)), ("delta", delta, (rows, dim))):
+        if tensor is None:
+            continue
+        if tensor.shape != shape or tensor.dtype != torch.float16 or not tensor.is_contiguous():
+            raise ValueError(f"{name} must be contiguous FP16 {list(shape)}")
+        _require_cuda(name, tensor, hidden.device)
+    check(lib.pkv_add_rms_norm(_ptr(hidden), _ptr(delta), _ptr(weight), _ptr(out), rows, dim, eps,
+                               _stream(hidden.device)))
+    return out
+
+
+def silu_mul(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
+    """``silu(gate) * up`` of FP16 gate_up [rows, 2 * inter] (gate first) into [rows, inter]."""
+    rows, width = gate_up.shape
+    if gate_up.dtype != torch.float16 or not gate_up.is_contiguous() or width % 2:
+        raise ValueError("gate_up must be contiguous FP16 [rows, 2 * inter]")
+    if out is None:
+        out = torch.empty((rows, width // 2), dtype=torch.float16, device=gate_up.device)
+    check(lib.pkv_silu_mul(_ptr(gate_up), _ptr(out), rows, width // 2, _stream(gate_up.device)))
+    return out

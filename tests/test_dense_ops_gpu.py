@@ -1,0 +1,68 @@
+"""Fused decoder-step kernels (csrc/dense_ops.cu) against the eager ops they replace.
+
+``add_rms_norm`` is the residual add followed by dense.rms_norm, and
+``silu_mul`` is SwiGLU's product (F.silu(gate) * up), each with the same FP16
+rounding points.  The residual add must match bit for bit.  The norm sums
+its squares in another order than torch's reduction; a last-bit difference
+in the FP32 scale can move the normalised value by one FP16 ulp, which the
+weight multiply (rounded again) can turn into two, on rare elements.  The
+SiLU product uses expf and IEEE division in FP32 as torch's kernel does, and
+is checked to one ulp.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from pagedcore_b200 import kernels
+from pagedcore_b200.dense import rms_norm
+from tests.conftest import cuda_device
+
+pytestmark = pytest.mark.gpu
+
+
+def ulp_close(actual: torch.Tensor, expected: torch.Tensor, ulps: int = 1) -> None:
+    a = actual.view(torch.int16).int()
+    b = expected.view(torch.int16).int()
+    assert int((a - b).abs().max()) <= ulps
+    assert float((a == b).float().mean()) > 0.99
+
+
+@pytest.mark.parametrize("rows", [1, 7, 256])
+def test_add_rms_norm_matches_the_eager_residual_add_and_norm(rows) -> None:
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(rows)
+    hidden = torch.randn(rows, 2048, dtype=torch.float16, device=device, generator=generator)
+    delta = torch.randn(rows, 2048, dtype=torch.float16, device=device, generator=generator)
+    weight = (1 + 0.1 * torch.randn(2048, device=device, generator=generator)).half()
+    expected_hidden = hidden + delta
+    expected = rms_norm(expected_hidden, weight)
+    out = torch.empty_like(hidden)
+    kernels.add_rms_norm(hidden, delta, weight, out)
+    assert torch.equal(hidden, expected_hidden)  # the residual add, in place
+    ulp_close(out, expected, ulps=2)
+    # Without delta: the norm alone, hidden untouched.
+    before = hidden.clone()
+    kernels.add_rms_norm(hidden, None, weight, out)
+    assert torch.equal(hidden, before)
+    ulp_close(out, rms_norm(before, weight), ulps=2)
+
+
+@pytest.mark.parametrize("inter", [32, 5632])
+def test_silu_mul_matches_the_eager_swiglu_product(inter) -> None:
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(inter)
+    gate_up = 3 * torch.randn(64, 2 * inter, dtype=torch.float16, device=device, generator=generator)
+    gate, up = gate_up.chunk(2, -1)
+    ulp_close(kernels.silu_mul(gate_up), F.silu(gate) * up)
+
+
+def test_fused_ops_reject_bad_shapes() -> None:
+    device = cuda_device()
+    hidden = torch.zeros(2, 2048, dtype=torch.float16, device=device)
+    with pytest.raises(ValueError, match="weight"):
+        kernels.add_rms_norm(hidden, None, torch.zeros(1024, dtype=torch.float16, device=device), hidden.clone())
+    with pytest.raises(ValueError, match="gate_up"):
+        kernels.silu_mul(torch.zeros(2, 7, dtype=torch.float16, device=device))
