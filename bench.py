@@ -850,6 +850,127 @@ def run_append_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def run_decoder_arm(args: argparse.Namespace) -> None:
+    """Row f1: the whole TinyLlama decoder step for config 4's batch, replayed as a CUDA graph.
+
+    Random-init TinyLlama weights (the reference publishes no checkpoint here),
+    256 sequences per GPU with contexts U[1, 2048 - room] filled with seeded
+    K/V, one greedy-free step = embedding, 22 x (norm, fused Q/K/V GEMM, fused
+    decode layer, output projection, norm, gate/up GEMM, SwiGLU product, down
+    projection), final norm and LM head (`DecoderStepGraph`).  Reported against
+    HBM: the bytes a step must move (weights read once, the attention's K/V
+    stream and the pool writes) over its time.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from pagedcore_b200 import workloads
+    from pagedcore_b200.decoder import BatchedDecoder
+    from pagedcore_b200.engine_types import KVReservation, RequestId
+    from pagedcore_b200.graph import DecoderStepGraph
+    from pagedcore_b200.kv_cache import KVAllocator
+    from pagedcore_b200.weights import random_weights
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    host_affinity = _bind_host_cores(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    seed = 4 + 1000 * rank
+    room = args.warmup + args.steps + 8
+    lengths = workloads.decode_lengths(seed, SEQUENCES, high=2048 - room).tolist()
+    need = sum(-(-(n + room) // 16) for n in lengths) + 8
+    pool = torch.empty((LAYERS, 2, need, 16, 4, 64), dtype=torch.float16, device=device)
+    allocator = KVAllocator(pool, validation="incremental", balance="measured")
+    requests = tuple(RequestId(f"s{i}") for i in range(SEQUENCES))
+    generator = torch.Generator(device=device).manual_seed(seed)
+    for request, length in zip(requests, lengths, strict=True):
+        allocator.create(KVReservation(request, -(-(length + room) // 16)))
+        kv = torch.randn(LAYERS, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
+        allocator.append(request, kv, kv, rotate=True)
+    weights = random_weights(seed, device)
+    decoder = BatchedDecoder(weights)
+    graph = DecoderStepGraph(decoder, allocator, rows=SEQUENCES)
+    ids = torch.randint(0, 32000, (SEQUENCES, 1), device=device, generator=generator)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(CALIBRATION_STEPS + args.warmup):
+        graph.step(ids, requests)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            logits = graph.step(ids, requests)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    step_ms = start.elapsed_time(end) / args.steps
+    allocator.check_device_errors()
+    # Bytes a step must move: every weight matrix once (the fused Q/K/V and
+    # gate/up copies are what the step reads), the embedding rows, and per
+    # layer the attention's K/V stream (the cached tokens, the new one
+    # included), its block tables, and the new token's K/V written.
+    cached = np.array([allocator.cached_length(r) for r in requests], dtype=np.int64)
+    weight_bytes = sum(t.numel() * t.element_size() for t in (*decoder.qkv, *decoder.gate_up)) + sum(
+        (layer.o_proj.numel() + layer.down_proj.numel() + 2 * layer.input_norm.numel()) * 2
+        for layer in weights.layers) + weights.lm_head.numel() * 2
+    kv_bytes = LAYERS * float((1024 * cached + 4 * ((cached + 15) // 16) + 1024).sum())
+    step_bytes = weight_bytes + kv_bytes + SEQUENCES * 2048 * 2
+    times = torch.tensor([step_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms = float(times.item())
+    if rank == 0:
+        peak, peak_kind = _peak_hbm()
+        achieved = step_bytes / (step_ms / 1000.0) / 1e9
+        line = {
+            "metric": "full TinyLlama decoder step tokens/s (row f1: batched decode step)",
+            "value": world * SEQUENCES / (step_ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (random-init TinyLlama weights N(0, 0.02), seeded K/V caches, random token ids)",
+            "config": {
+                "workload": f"{SEQUENCES} sequences per GPU, contexts U[1, {2048 - room}], one token each per step "
+                            "through the whole decoder (22 layers + LM head); each step replayed as one CUDA graph "
+                            "(DecoderStepGraph)",
+                "parallelism": f"dp{world} (independent sequences, weights replicated, no collective)",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "whole decoder step (GEMMs, fused decode layers, norms)",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "bytes_per_step": step_bytes,
+                "weight_bytes": weight_bytes,
+                "attention_bytes": kv_bytes,
+                "traffic": None,
+            },
+            "logits_finite": bool(torch.isfinite(logits).all().item()),
+            "clocks": clocks.summary(),
+            "host_affinity": host_affinity,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -859,9 +980,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
-    parser.add_argument("--workload", choices=("decode", "stress", "append"), default="decode",
+    parser.add_argument("--workload", choices=("decode", "stress", "append", "decoder"), default="decode",
                         help="decode: config 4 (the headline line); stress: config 5 (allocator churn); "
-                             "append: config 2a (prompt K/V appends)")
+                             "append: config 2a (prompt K/V appends); decoder: row f1 (whole decoder step)")
     parser.add_argument("--stress-iterations", type=int, default=300)
     parser.add_argument("--stress-warmup", type=int, default=200)
     args = parser.parse_args()
@@ -874,6 +995,8 @@ def main() -> None:
         run_stress_arm(args)
     elif args.workload == "append":
         run_append_arm(args)
+    elif args.workload == "decoder":
+        run_decoder_arm(args)
     else:
         run_gpu_arm(args)
 
