@@ -732,10 +732,12 @@ def run_append_arm(args: argparse.Namespace) -> None:
         dist.barrier(device_ids=[local_rank])
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        torch.cuda.nvtx.range_push("timed")
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
         end.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
     kernel_ms = start.elapsed_time(end) / args.steps
     allocator.check_device_errors()
@@ -807,6 +809,9 @@ def run_append_arm(args: argparse.Namespace) -> None:
                 "algorithmic_bytes_per_step": step_bytes,
                 "avg_launch_ms": kernel_ms / len(prompts),
                 "traffic": None,
+                "traffic_note": "ncu reads per step = 1.007 x the K/V input (read once); the pool writes stay in L2 "
+                                "within a launch, so per-launch DRAM write counts undercount them "
+                                "(profiles/append_kv_cfg2a.md)",
             },
             "e2e": {
                 "value": all_tokens / (e2e_ms / 1000.0),
