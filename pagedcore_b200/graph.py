@@ -36,6 +36,18 @@ from pagedcore_b200.kv_cache import KVAllocator
 _LAYERS = 22
 
 
+def _replay_args(allocator: KVAllocator, rows: int, grid: int) -> tuple:
+    """Fixed pkv_decode_layer arguments of the staged (padded) step, minus layer, I/O and stream.
+
+    With piece tables the kernels take the block count only as a bound and
+    ignore the arithmetic partition, so the upload's room and constants stand
+    in for them: the arguments repeat from step to step and key the graphs.
+    """
+    staged = allocator._staged
+    fixed = allocator._decode_layer_args(staged.staged_batch, rows, grid)
+    return (*fixed[:8], staged.flat_capacity, grid, 1, grid, 1, *fixed[13:16])
+
+
 class DecodeStepGraph:
     """Decode steps of up to ``rows`` requests through captured CUDA graphs.
 
@@ -114,11 +126,7 @@ class DecodeStepGraph:
         self._check(query, key, value, out)
         with allocator.append_decode(requests, layout=(self.rows, self.grid)):
             staged = allocator._staged
-            fixed = allocator._decode_layer_args(staged.staged_batch, self.rows, self.grid)
-            # With piece tables the kernels take the block count only as a
-            # bound and ignore the arithmetic partition: pass the upload's
-            # room and constants, so the arguments repeat from step to step.
-            args = (*fixed[:8], staged.flat_capacity, self.grid, 1, self.grid, 1, *fixed[13:16])
+            args = _replay_args(allocator, self.rows, self.grid)
             cache_key = (args, query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr())
             graph = self._graphs.get(cache_key)
             if graph is None:
@@ -136,11 +144,11 @@ class DecodeStepGraph:
 class DecoderStepGraph:
     """``BatchedDecoder`` steps of up to ``rows`` requests replayed as CUDA graphs.
 
-    A decoder step launches about a dozen kernels per layer (norms, the fused
-    Q/K/V and gate/up GEMMs, the decode layer, the output and down
-    projections, residual adds) plus the embedding and the logits: over 300
-    launches whose Python and launch costs exceed the GPU time at small
-    batches.  Here the whole step, ``BatchedDecoder.forward`` with the fused
+    A decoder step launches nine kernels per layer (two residual-add norms,
+    the fused Q/K/V and gate/up GEMMs, the decode layer's split and combine,
+    the output and down projections, the SwiGLU product) plus the embedding,
+    the final norm and the logits: about 200 launches whose Python and launch
+    costs exceed the GPU time at small batches.  Here the whole step, ``BatchedDecoder.forward`` with the fused
     decode layer launched on the step's padded tables, is captured once per
     upload buffer and replayed: the host stages the step (ledger, tables, one
     upload), copies the token ids into a fixed buffer and launches the graph.
@@ -212,8 +220,7 @@ class DecoderStepGraph:
             raise ValueError("input_ids must be int64 [batch, 1] matching request IDs on the pool device")
         with allocator.append_decode(requests, layout=(self.rows, self.grid)):
             staged = allocator._staged
-            fixed = allocator._decode_layer_args(staged.staged_batch, self.rows, self.grid)
-            args = (*fixed[:8], staged.flat_capacity, self.grid, 1, self.grid, 1, *fixed[13:16])
+            args = _replay_args(allocator, self.rows, self.grid)
             entry = self._graphs.get(args)
             if entry is None:
                 if len(self._graphs) >= self.max_graphs:
