@@ -204,6 +204,32 @@ class PrefillAppend:
         return self._allocator.attend(self.batch, query, layer_index=layer, out=out)
 
 
+def padded_tables(
+    pieces: np.ndarray, row_pieces: np.ndarray, host: np.ndarray, count: int, total: int, rows: int, grid: int
+) -> np.ndarray:
+    """A batch's step tables in the padded layout of ``rows`` rows and ``grid`` pieces.
+
+    pieces [p][4] and row_pieces [count][2] from ``kernels.decode_tables``;
+    host = lengths [count] | prefix [count + 1] | flat [total].  Layout:
+    pieces [grid][4] | row_pieces [rows][2] | lengths [rows] | prefix [rows + 1]
+    | flat [total], padded with empty pieces (0, 0, 0, 0), rows without pieces
+    (0, 0), length 0 and prefix ``total``, which every kernel skips.
+    """
+    if count > rows or len(pieces) > grid:
+        raise ValueError(f"the batch needs {count} rows and {len(pieces)} pieces; the layout has {rows} and {grid}")
+    tables = np.zeros(4 * grid + 4 * rows + 1 + total, dtype=np.int32)
+    tables[: 4 * len(pieces)] = pieces.reshape(-1)
+    at = 4 * grid
+    tables[at : at + 2 * count] = row_pieces.reshape(-1)
+    at += 2 * rows
+    tables[at : at + count] = host[:count]  # lengths
+    at += rows
+    tables[at : at + count + 1] = host[count : 2 * count + 1]  # prefix
+    tables[at + count + 1 : at + rows + 1] = total
+    tables[at + rows + 1 :] = host[2 * count + 1 : 2 * count + 1 + total]  # flat
+    return tables
+
+
 @dataclass(slots=True)
 class _SlotSpeeds:
     """Per-CTA-slot weights of the decode pieces, from measured wall times."""
@@ -797,20 +823,7 @@ class KVAllocator:
         if layout is None:
             tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), host[: 2 * count + 1 + total]))
             return tables, total, plan
-        rows, grid = layout
-        if plan.grid > grid:
-            raise ValueError(f"the batch's plan needs {plan.grid} pieces; the layout has {grid}")
-        tables = np.zeros(4 * grid + 4 * rows + 1 + total, dtype=np.int32)
-        tables[: 4 * plan.grid] = pieces.reshape(-1)
-        at = 4 * grid
-        tables[at : at + 2 * count] = row_pieces.reshape(-1)
-        at += 2 * rows
-        tables[at : at + count] = host[:count]  # lengths
-        at += rows
-        tables[at : at + count + 1] = host[count : 2 * count + 1]  # prefix
-        tables[at + count + 1 : at + rows + 1] = total
-        tables[at + rows + 1 :] = host[2 * count + 1 : 2 * count + 1 + total]  # flat
-        return tables, total, plan
+        return padded_tables(pieces, row_pieces, host, count, total, *layout), total, plan
 
     @staticmethod
     def _device_batch(

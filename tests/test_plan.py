@@ -108,6 +108,30 @@ def test_tables_follow_the_weights() -> None:
     assert np.array_equal(again[0], pieces) and np.array_equal(again[1], row_pieces)
 
 
+def test_padded_tables_put_every_region_at_its_fixed_offset() -> None:
+    from pagedcore_b200.kv_cache import padded_tables
+
+    lengths = np.array([5, 40, 17], dtype=np.int32)
+    prefix = np.concatenate(([0], np.cumsum((lengths + 15) // 16))).astype(np.int32)
+    total = int(prefix[-1])
+    flat = np.arange(100, 100 + total, dtype=np.int32)
+    pieces, row_pieces = kernels.decode_tables(prefix, 2)
+    rows, grid = 8, 6
+    tables = padded_tables(pieces, row_pieces, np.concatenate((lengths, prefix, flat)), 3, total, rows, grid)
+    assert len(tables) == 4 * grid + 4 * rows + 1 + total
+    assert np.array_equal(tables[:8].reshape(2, 4), pieces) and not tables[8 : 4 * grid].any()  # empty pieces
+    at = 4 * grid
+    padded_rows = tables[at : at + 2 * rows].reshape(rows, 2)
+    assert np.array_equal(padded_rows[:3], row_pieces) and not padded_rows[3:].any()  # rows with no pieces
+    at += 2 * rows
+    assert tables[at : at + rows].tolist() == [5, 40, 17, 0, 0, 0, 0, 0]
+    at += rows
+    assert tables[at : at + rows + 1].tolist() == prefix.tolist() + [total] * (rows - 3)
+    assert np.array_equal(tables[at + rows + 1 :], flat)
+    with pytest.raises(ValueError, match="layout has 2 and 6"):
+        padded_tables(pieces, row_pieces, np.concatenate((lengths, prefix, flat)), 3, total, 2, grid)
+
+
 def test_tables_reject_bad_arguments() -> None:
     prefix = random_prefix(5, 4, max_blocks=3)
     with pytest.raises(ValueError, match="grid must lie"):
