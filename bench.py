@@ -155,6 +155,8 @@ def _config(n_gpus: int) -> dict:
                     "run's appends], churned block tables; one step = staged append + 22 fused decode-layer launches (Q/K RoPE, "
                     "new-token KV write, split-K GQA decode attention) + commit; dense GEMMs not included",
         "sequences_per_gpu": SEQUENCES,
+        "sharing": "BASELINE config 4 spreads 256 sequences over the N GPUs; this line keeps 256 per GPU so "
+                   "per-GPU work is fixed as N grows (weak scaling); --sequences 256/N gives the shared-batch point",
         "layers": LAYERS,
         "heads": "32 query / 4 KV, head_dim 64, block 16",
         "l2": "inputs larger than L2: each attention launch streams ~0.25 GB of K/V (L2 is 126 MB)",
