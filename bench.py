@@ -553,8 +553,8 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                 "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": d2h_bytes,
                 "path": "pinned host Q/K/V -> device and attention outputs -> pinned host every step, on two "
-                        "copy streams overlapped with the neighbouring steps; KVAllocator.append_decode + "
-                        "decode_layer per layer",
+                        "copy streams overlapped with the neighbouring steps; DecodeStepGraph.step "
+                        "(KVAllocator.append_decode and the 22 decode layers replayed as one CUDA graph)",
             },
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
