@@ -23,7 +23,7 @@ _KV_HEADS = 4
 _QUERY_HEADS = 32
 _HEAD_DIM = 64
 _PARTIAL_BYTES = _QUERY_HEADS * (_HEAD_DIM + 2) * 4  # one split partial: (m, l, O) of 32 heads, FP32
-_CLAIM_BYTES = 2 * 256 * 4  # two sets of per-SM slot-claim counters and a launch's exit count
+CLAIM_BYTES = 2 * 256 * 4  # the workspace's two sets of 256 per-SM slot-claim counters (int32)
 
 
 def workspace_bytes(batch: int, grid: int) -> int:
@@ -31,7 +31,7 @@ def workspace_bytes(batch: int, grid: int) -> int:
     four uint32 wall-time counters per slot, then a split partial per (row,
     piece) slot (batch + grid).  It must be zero before its first use; the
     kernels leave the claim counters at zero."""
-    return _CLAIM_BYTES + grid * 16 + (batch + grid) * _PARTIAL_BYTES
+    return CLAIM_BYTES + grid * 16 + (batch + grid) * _PARTIAL_BYTES
 
 
 def _ptr(tensor: Tensor | None) -> ctypes.c_void_p:

@@ -337,7 +337,7 @@ class KVAllocator:
         workspace = self._workspace_for(plan.workspace_bytes)
         if workspace is None:
             return None
-        start = kernels._CLAIM_BYTES // 4
+        start = kernels.CLAIM_BYTES // 4
         return workspace[start : start + 4 * plan.grid].view(torch.int32)
 
     def _slot_weights(self, plan: kernels.DecodePlan) -> np.ndarray | None:
@@ -362,7 +362,7 @@ class KVAllocator:
     def _reset_slot_counters(self, grid: int) -> None:
         """Zero every slot's counters: the next window holds launches of ``grid`` only."""
         if self._workspace is not None:
-            start = kernels._CLAIM_BYTES // 4
+            start = kernels.CLAIM_BYTES // 4
             self._workspace[start : start + 4 * kernels.decode_slots(self._pool.device)].zero_()
         self._window_grid = grid
 
