@@ -654,12 +654,13 @@ def run_append_arm(args: argparse.Namespace) -> None:
     """BASELINE config 2(a): prompt K/V appends with fused K-RoPE after allocator churn.
 
     A 4096-block pool fragmented by the seeded 10k-op churn, then 8 prompts of
-    U[1, 2047] tokens.  `value` times the append kernel (`pkv_append_kv`, K
-    rotated at its positions, K and V scattered through the prompt's slots)
-    over the 8 prompts with K/V resident in HBM; `e2e` times the public
-    `KVAllocator.append(..., rotate=True)` with every prompt's K/V copied in
-    from pinned host memory, the requests released and re-created around it,
-    and the device error flag read back per step.
+    U[1, 2047] tokens, written by one batched append.  `value` times that
+    append's kernel (`pkv_append_kv`, K rotated at its positions, K and V
+    scattered through the prompts' slots, one launch for all 8) with K/V
+    resident in HBM; `e2e` times the public `KVAllocator.append_many(...,
+    rotate=True)` with the prompts' K/V copied in from pinned host memory,
+    the requests released and re-created around it, and the device error
+    flag read back per step.
     """
     import torch
     import torch.distributed as dist
@@ -690,45 +691,37 @@ def run_append_arm(args: argparse.Namespace) -> None:
             allocator.append(request, fill[:, : op.tokens], fill[:, : op.tokens])
         else:
             allocator.release_all(request)
-    prompts = []
-    for prompt in case.prompts:
-        request = RequestId(f"prompt{prompt.request}")
-        key_host = torch.from_numpy(prompt.key).pin_memory()
-        value_host = torch.from_numpy(prompt.value).pin_memory()
-        key, value = key_host.to(device), value_host.to(device)
-        allocator.create(KVReservation(request, prompt.credits))
-        allocator.append(request, key, value, rotate=True)
-        tokens = key.shape[1]
+    # The 8 prompts are written by one batched append (KVAllocator.append_many):
+    # their tokens concatenated in request order, one kernel launch.
+    requests = [RequestId(f"prompt{prompt.request}") for prompt in case.prompts]
+    credits = [prompt.credits for prompt in case.prompts]
+    counts = [prompt.key.shape[1] for prompt in case.prompts]
+    key_host = torch.from_numpy(np.concatenate([p.key for p in case.prompts], axis=1)).pin_memory()
+    value_host = torch.from_numpy(np.concatenate([p.value for p in case.prompts], axis=1)).pin_memory()
+    key, value = key_host.to(device), value_host.to(device)
+    for request, credit in zip(requests, credits, strict=True):
+        allocator.create(KVReservation(request, credit))
+    allocator.append_many(requests, key, value, counts, rotate=True)
+    slots, positions = [], []
+    for request, count in zip(requests, counts, strict=True):
         table = np.asarray(allocator.block_table(request), dtype=np.int64)
-        positions = np.arange(tokens, dtype=np.int32)
-        slots = (table[positions // 16] * 16 + positions % 16).astype(np.int32)
-        prompts.append((request, prompt.credits, key, value, key_host, value_host,
-                        torch.from_numpy(slots).to(device), torch.from_numpy(positions).to(device)))
-    total_tokens = sum(p[2].shape[1] for p in prompts)
+        position = np.arange(count, dtype=np.int32)
+        slots.append((table[position // 16] * 16 + position % 16).astype(np.int32))
+        positions.append(position)
+    slots_device = torch.from_numpy(np.concatenate(slots)).to(device)
+    positions_device = torch.from_numpy(np.concatenate(positions)).to(device)
+    total_tokens = sum(counts)
     # Algorithmic bytes: per (layer, token) K and V read and written (4 x 512 B);
     # per token its slot and position and one RoPE row (32 cos + 32 sin FP16).
     step_bytes = total_tokens * (LAYERS * 4 * 512 + 8 + 128)
     stream = torch.cuda.current_stream(device)
 
     def kernel_step() -> None:
-        for _, _, key, value, _, _, slots, positions in prompts:
-            kernels.append_kv(pool, key, value, slots, layer_begin=0, error_flag=allocator._error,
-                              positions=positions, rope_table=allocator._rope)
+        kernels.append_kv(pool, key, value, slots_device, layer_begin=0, error_flag=allocator._error,
+                          positions=positions_device, rope_table=allocator._rope)
 
     for _ in range(args.warmup):
         kernel_step()
-    torch.cuda.synchronize(device)
-    # The step's launches replay as one CUDA graph: each kernels.append_kv
-    # call costs 15-20 us of Python and ctypes on the host, more than most of
-    # these launches take on the GPU, and `value` is the device's throughput.
-    side = torch.cuda.Stream(device)
-    side.wait_stream(stream)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=side):
-        kernel_step()
-    stream.wait_stream(side)
-    for _ in range(args.warmup):
-        graph.replay()
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -737,7 +730,7 @@ def run_append_arm(args: argparse.Namespace) -> None:
         torch.cuda.nvtx.range_push("timed")
         start.record(stream)
         for _ in range(args.steps):
-            graph.replay()
+            kernel_step()
         end.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
@@ -745,16 +738,16 @@ def run_append_arm(args: argparse.Namespace) -> None:
     allocator.check_device_errors()
 
     # End to end through the public API, K/V from pinned host memory.
-    staging = [(torch.empty_like(p[2]), torch.empty_like(p[3])) for p in prompts]
+    key_staging, value_staging = torch.empty_like(key), torch.empty_like(value)
 
     def public_step() -> None:
-        for request, _, _, _, _, _, _, _ in prompts:
+        for request in requests:
             allocator.release_all(request)
-        for (request, credits, _, _, key_host, value_host, _, _), (key, value) in zip(prompts, staging):
-            allocator.create(KVReservation(request, credits))
-            key.copy_(key_host, non_blocking=True)
-            value.copy_(value_host, non_blocking=True)
-            allocator.append(request, key, value, rotate=True)
+        for request, credit in zip(requests, credits, strict=True):
+            allocator.create(KVReservation(request, credit))
+        key_staging.copy_(key_host, non_blocking=True)
+        value_staging.copy_(value_host, non_blocking=True)
+        allocator.append_many(requests, key_staging, value_staging, counts, rotate=True)
         allocator.check_device_errors()  # the step's device-to-host read
 
     for _ in range(args.warmup):
@@ -792,13 +785,13 @@ def run_append_arm(args: argparse.Namespace) -> None:
             "data": "synthetic (seeded K/V ~N(0,1), prompt lengths U[1, 2047]); the reference publishes no inputs",
             "config": {
                 "workload": f"config 2a per GPU: pool of {case.num_blocks} blocks after a seeded "
-                            f"{len(case.churn)}-op alloc/free churn, {len(prompts)} prompts ({total_tokens} tokens "
-                            "on rank 0) appended with K rotated at positions 0..T-1; one step = all prompts",
+                            f"{len(case.churn)}-op alloc/free churn, {len(requests)} prompts ({total_tokens} tokens "
+                            "on rank 0) appended with K rotated at positions 0..T-1; one step = all prompts in one "
+                            "batched append (KVAllocator.append_many: one kernel launch)",
                 "l2": f"inputs larger than L2: each step reads {2 * LAYERS * total_tokens * 512 / 1e6:.0f} MB of "
                       "K/V (L2 is 126 MB)",
                 "parallelism": f"dp{world} (independent prompts, one KV pool per GPU, no collective)",
-                "launch": "the step's 8 append launches replayed as one CUDA graph (value); e2e makes the "
-                          "public calls",
+                "launch": "one append launch per step (value); e2e makes the public calls",
             },
             "roofline": {
                 "bound": "hbm",
@@ -809,7 +802,7 @@ def run_append_arm(args: argparse.Namespace) -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "algorithmic_bytes_per_step": step_bytes,
-                "avg_launch_ms": kernel_ms / len(prompts),
+                "avg_launch_ms": kernel_ms,
                 "traffic": None,
                 "traffic_note": "ncu reads per step = 1.007 x the K/V input (read once); the pool writes stay in L2 "
                                 "within a launch, so per-launch DRAM write counts undercount them "
@@ -820,10 +813,10 @@ def run_append_arm(args: argparse.Namespace) -> None:
                 "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * LAYERS * total_tokens * 512 + 8 * total_tokens,
                 "d2h_bytes_per_step": 4,
-                "path": "KVAllocator.release_all + create + append(rotate=True) per prompt, K/V copied from pinned "
-                        "host memory each step, error flag read back per step",
+                "path": "KVAllocator.release_all + create per prompt, then append_many(rotate=True) of the 8 "
+                        "prompts, K/V copied from pinned host memory each step, error flag read back per step",
             },
-            "gpu_launches": args.steps * len(prompts),
+            "gpu_launches": args.steps,
             "clocks": clocks.summary(),
             "host_affinity": host_affinity,
         }
@@ -836,9 +829,9 @@ def run_append_arm(args: argparse.Namespace) -> None:
             begin = time.perf_counter()
             repeats = 0
             while time.perf_counter() - begin < 10.0:
-                for prompt, entry in zip(sample, prompts):
+                for prompt, prompt_slots in zip(sample, slots, strict=False):
                     tokens = prompt.key.shape[1]
-                    kv_write.append_rotated(host_pool, prompt.key, prompt.value, entry[6].cpu().numpy(),
+                    kv_write.append_rotated(host_pool, prompt.key, prompt.value, prompt_slots,
                                             np.arange(tokens, dtype=np.int32), table)
                 repeats += 1
             seconds = time.perf_counter() - begin

@@ -97,6 +97,19 @@ int pkv_ledger_append_plan(pkv_ledger *ledger, int64_t request, int32_t tokens,
                            int32_t *out_slots, int32_t *out_start_position);
 int pkv_ledger_append_commit(pkv_ledger *ledger, int64_t request, int32_t tokens);
 
+/* Several KVAllocator.append calls at once, for a batched write of several
+ * prompts in one kernel launch.  Request i (all distinct) is planned as if
+ * requests 0..i-1 had been committed before it, so the slots are those that
+ * the same appends made one after another would get; out_slots receives
+ * tokens[0] + ... + tokens[count-1] slot ids in request order and
+ * out_start_positions[i] each request's first position.  No state changes
+ * until commit_many, which checks every request before changing any (a
+ * failing batch changes nothing). */
+int pkv_ledger_append_plan_many(pkv_ledger *ledger, const int64_t *requests, const int32_t *tokens,
+                                int32_t count, int32_t *out_slots, int32_t *out_start_positions);
+int pkv_ledger_append_commit_many(pkv_ledger *ledger, const int64_t *requests, const int32_t *tokens,
+                                  int32_t count);
+
 /* KVAllocator.append_decode (kv_cache.py:181-219): stage length+1 for each
  * request, borrowing free[-1], free[-2], ... in request order for requests
  * whose length is a multiple of 16.  Writes each row's slot id and RoPE

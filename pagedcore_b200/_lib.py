@@ -48,6 +48,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_ledger_table": (c_int, [c_void_p, c_int64, i32p, c_int32, i32p]),
     "pkv_ledger_append_plan": (c_int, [c_void_p, c_int64, c_int32, c_void_p, i32p]),
     "pkv_ledger_append_commit": (c_int, [c_void_p, c_int64, c_int32]),
+    "pkv_ledger_append_plan_many": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
+    "pkv_ledger_append_commit_many": (c_int, [c_void_p, c_void_p, c_void_p, c_int32]),
     "pkv_ledger_decode_begin": (c_int, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
     "pkv_ledger_decode_check": (c_int, [c_void_p, c_int64, c_int32, i32p, i32p]),
     "pkv_ledger_decode_mark": (c_int, [c_void_p, c_int64, c_int32]),

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <string>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "pagedkv.h"
@@ -365,6 +366,105 @@ int pkv_ledger_append_commit(pkv_ledger *L, int64_t request, int32_t tokens) {
     L->live += tokens;
     s.length = static_cast<int32_t>(length);
     return audit(L, &request, 1);
+}
+
+// Several appends in one call: request i is planned as if requests 0..i-1 of
+// the call had been committed before it, so its new blocks continue down the
+// free stack below theirs (the order in which sequential appends would take
+// them).  Nothing changes until commit_many, which checks every request
+// before it changes any.
+namespace {
+
+int check_distinct(const int64_t *requests, int32_t count) {
+    std::unordered_set<int64_t> seen;
+    for (int32_t i = 0; i < count; ++i) {
+        if (!seen.insert(requests[i]).second) {
+            return fail(PKV_VALUE_ERROR, "a request may appear only once in a batched append");
+        }
+    }
+    return PKV_OK;
+}
+
+}  // namespace
+
+int pkv_ledger_append_plan_many(pkv_ledger *L, const int64_t *requests, const int32_t *tokens, int32_t count,
+                                int32_t *out_slots, int32_t *out_start_positions) {
+    pkv::clear_error();
+    int rc = check_mutation(L);
+    if (rc) return rc;
+    if (count < 1) return fail(PKV_VALUE_ERROR, "a batched append needs at least one request");
+    if ((rc = check_distinct(requests, count))) return rc;
+    if ((rc = audit(L, requests, count))) return rc;
+    const size_t top = L->free_stack.size();
+    size_t taken = 0;  // blocks the earlier requests of this call take from the top
+    int64_t at = 0;
+    for (int32_t i = 0; i < count; ++i) {
+        auto it = L->sequences.find(requests[i]);
+        if (it == L->sequences.end()) return key_error(requests[i]);
+        const Sequence &s = it->second;
+        if (tokens[i] < 1) {
+            return fail(PKV_VALUE_ERROR, "K and V must share FP16 [22, tokens, 4, 64] on the pool device");
+        }
+        const int64_t length = static_cast<int64_t>(s.length) + tokens[i];
+        if (length > kContextLimit) return fail(PKV_VALUE_ERROR, "KV cache must not exceed 2048 token positions");
+        const int32_t required = blocks_for(length);
+        if (required > s.credits) return fail(PKV_RUNTIME_ERROR, "KV append exceeds request reservation");
+        const int32_t additional = required - static_cast<int32_t>(s.blocks.size());
+        if (static_cast<size_t>(additional) > top - taken) {
+            return fail(PKV_RUNTIME_ERROR, "KV pool has insufficient free blocks");
+        }
+        for (int32_t t = 0; t < tokens[i]; ++t) {
+            const int32_t position = s.length + t;
+            const int32_t logical = position / kBlockTokens;
+            const int32_t physical =
+                logical < static_cast<int32_t>(s.blocks.size())
+                    ? s.blocks[logical]
+                    : L->free_stack[top - 1 - taken - (logical - s.blocks.size())];
+            out_slots[at + t] = physical * kBlockTokens + position % kBlockTokens;
+        }
+        if (out_start_positions) out_start_positions[i] = s.length;
+        taken += additional;
+        at += tokens[i];
+    }
+    return PKV_OK;
+}
+
+int pkv_ledger_append_commit_many(pkv_ledger *L, const int64_t *requests, const int32_t *tokens, int32_t count) {
+    pkv::clear_error();
+    int rc = check_mutation(L);
+    if (rc) return rc;
+    if (count < 1) return fail(PKV_VALUE_ERROR, "a batched append needs at least one request");
+    if ((rc = check_distinct(requests, count))) return rc;
+    size_t taken = 0;
+    for (int32_t i = 0; i < count; ++i) {
+        auto it = L->sequences.find(requests[i]);
+        if (it == L->sequences.end()) return key_error(requests[i]);
+        const Sequence &s = it->second;
+        const int64_t length = static_cast<int64_t>(s.length) + tokens[i];
+        if (tokens[i] < 1 || length > kContextLimit) return fail(PKV_VALUE_ERROR, "invalid KV append commit");
+        const int32_t required = blocks_for(length);
+        const int32_t additional = required - static_cast<int32_t>(s.blocks.size());
+        if (required > s.credits || static_cast<size_t>(additional) > L->free_stack.size() - taken) {
+            return fail(PKV_RUNTIME_ERROR, "KV append exceeds request reservation");
+        }
+        taken += additional;
+    }
+    for (int32_t i = 0; i < count; ++i) {
+        Sequence &s = L->sequences.find(requests[i])->second;
+        const int64_t length = static_cast<int64_t>(s.length) + tokens[i];
+        const int32_t additional = blocks_for(length) - static_cast<int32_t>(s.blocks.size());
+        // kv_cache.py:175-178 for each request in order: pop its new blocks (top first).
+        for (int32_t b = 0; b < additional; ++b) {
+            const int32_t block = L->free_stack.back();
+            L->free_stack.pop_back();
+            s.blocks.push_back(block);
+            L->owner[block] = requests[i];
+        }
+        L->owned += additional;
+        L->live += tokens[i];
+        s.length = static_cast<int32_t>(length);
+    }
+    return audit(L, requests, count);
 }
 
 int pkv_ledger_decode_begin(pkv_ledger *L, const int64_t *requests, int32_t count,

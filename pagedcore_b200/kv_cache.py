@@ -475,6 +475,64 @@ class KVAllocator:
         # Publish valid positions only after both K and V writes were issued.
         self._ledger.append_commit(handle, tokens)
 
+    @torch.inference_mode()
+    def append_many(
+        self,
+        request_ids: Sequence[RequestId],
+        key: Tensor,
+        value: Tensor,
+        tokens: Sequence[int],
+        *,
+        rotate: bool = False,
+    ) -> None:
+        """``append`` for several requests in one kernel launch.
+
+        key/value FP16 [22, sum(tokens), 4, 64] hold the requests' tokens
+        concatenated in request order (``tokens[i]`` positions for request i).
+        Same slots and pool bytes as calling ``append`` for each request in
+        order, and all or nothing: if any request's append would fail, no
+        request changes.  Requests must be distinct.
+        """
+        self._check_worker()
+        if self._ledger.staging:
+            raise RuntimeError("KV mutation is not allowed during a staged decode append")
+        request_ids = tuple(request_ids)
+        counts = [int(t) for t in tokens]
+        if not request_ids or len(counts) != len(request_ids):
+            raise ValueError("append_many takes one token count per request")
+        missing = next((request_id for request_id in request_ids if request_id not in self._handles), None)
+        if missing is not None:
+            raise KeyError(missing)
+        handles = np.array([self._handles[request_id] for request_id in request_ids], dtype=np.int64)
+        total = sum(counts)
+        if (
+            key.ndim != 4
+            or key.shape[0] != 22
+            or key.shape[1] != total
+            or key.shape[2:] != (4, 64)
+            or value.shape != key.shape
+            or key.dtype != torch.float16
+            or value.dtype != torch.float16
+            or key.device != self._pool.device
+            or value.device != self._pool.device
+        ):
+            raise ValueError("K and V must share FP16 [22, sum(tokens), 4, 64] on the pool device")
+        slots, starts = self._ledger.append_plan_many(handles, counts)
+        if rotate:
+            positions = np.concatenate(
+                [np.arange(start, start + count, dtype=np.int32) for start, count in zip(starts, counts, strict=True)]
+            )
+            meta = self._upload_i32(slots, positions)
+            kernels.append_kv(
+                self._pool, key, value, meta[:total], layer_begin=0, error_flag=self._error,
+                positions=meta[total:], rope_table=self._rope,
+            )
+        else:
+            meta = self._upload_i32(slots)
+            kernels.append_kv(self._pool, key, value, meta, layer_begin=0, error_flag=self._error)
+        # Publish every request only after the one launch was issued.
+        self._ledger.append_commit_many(handles, counts)
+
     @contextmanager
     def prefill_append(self, request_id: RequestId, tokens: int) -> Iterator[PrefillAppend]:
         """Append a prompt chunk layer by layer, attending to it through the pool.

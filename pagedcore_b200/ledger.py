@@ -87,6 +87,28 @@ class BlockLedger:
         self.append_commit(request, tokens)
         return slots
 
+    def append_plan_many(self, requests: Sequence[int], tokens: Sequence[int]) -> tuple[np.ndarray, np.ndarray]:
+        """Slot ids of several appends planned in order (request i as if 0..i-1 were committed).
+
+        Returns the slots of all requests concatenated and each request's first position.
+        """
+        handles = np.ascontiguousarray(requests, dtype=np.int64)
+        counts = np.ascontiguousarray(tokens, dtype=np.int32)
+        if handles.shape != counts.shape or handles.ndim != 1:
+            raise ValueError("requests and tokens must be two sequences of one length")
+        slots = np.empty(max(int(counts.sum()), 1), dtype=np.int32)
+        starts = np.empty(max(len(handles), 1), dtype=np.int32)
+        check(lib.pkv_ledger_append_plan_many(self._handle, handles.ctypes.data, counts.ctypes.data, len(handles),
+                                              _i32(slots), _i32(starts)))
+        return slots[: int(counts.sum())], starts[: len(handles)]
+
+    def append_commit_many(self, requests: Sequence[int], tokens: Sequence[int]) -> None:
+        handles = np.ascontiguousarray(requests, dtype=np.int64)
+        counts = np.ascontiguousarray(tokens, dtype=np.int32)
+        if handles.shape != counts.shape or handles.ndim != 1:
+            raise ValueError("requests and tokens must be two sequences of one length")
+        check(lib.pkv_ledger_append_commit_many(self._handle, handles.ctypes.data, counts.ctypes.data, len(handles)))
+
     # -- staged one-token decode -------------------------------------------
     def decode_begin(self, requests: Sequence[int]) -> tuple[np.ndarray, np.ndarray]:
         handles = np.asarray(requests, dtype=np.int64)

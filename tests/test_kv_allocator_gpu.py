@@ -103,6 +103,51 @@ def test_config2_append_matches_reference_pool(append_golden: dict) -> None:
         assert list(allocator.block_table(request)) == append_golden["after_decode"]["tables"][request]
 
 
+def test_config2_prompts_in_one_batched_append_match_reference_pool(append_golden: dict) -> None:
+    """append_many of config 2's 8 prompts in one launch gives the reference's pool bytes."""
+    device = cuda_device()
+    case = workloads.append_case()
+    allocator = KVAllocator(nan_pool(case.num_blocks, device), validation="incremental")
+    for index, op in enumerate(case.churn):
+        rid = RequestId(str(op.request))
+        if op.kind == "create":
+            allocator.create(KVReservation(rid, op.credits))
+            key, value = workloads.churn_fill(index, op.tokens)
+            allocator.append(rid, torch.from_numpy(key).to(device), torch.from_numpy(value).to(device))
+        else:
+            allocator.release_all(rid)
+    requests = [RequestId(str(prompt.request)) for prompt in case.prompts]
+    for request, prompt in zip(requests, case.prompts, strict=True):
+        allocator.create(KVReservation(request, prompt.credits))
+    key = torch.from_numpy(np.concatenate([p.key for p in case.prompts], axis=1)).to(device)
+    value = torch.from_numpy(np.concatenate([p.value for p in case.prompts], axis=1)).to(device)
+    allocator.append_many(requests, key, value, [p.key.shape[1] for p in case.prompts], rotate=True)
+    counts = allocator.capacity()
+    assert sha256(allocator.pool.cpu().numpy()) == append_golden["after_prompts"]["pool_sha256"]
+    assert [counts.total_blocks, counts.free_blocks, counts.owned_blocks, counts.reserved_blocks,
+            counts.active_slots, counts.live_cached_token_slots] == append_golden["after_prompts"]["capacity"]
+    allocator.check_device_errors()
+
+
+def test_a_failing_batched_append_writes_and_publishes_nothing() -> None:
+    device = cuda_device()
+    allocator = KVAllocator(nan_pool(8, device))
+    allocator.create(KVReservation(RequestId("a"), 2))
+    allocator.create(KVReservation(RequestId("b"), 1))
+    key, value = kv_values(40, device=device)
+    counts = allocator.capacity()
+    with pytest.raises(RuntimeError, match="exceeds request reservation"):  # b holds 16 positions
+        allocator.append_many([RequestId("a"), RequestId("b")], key, value, [20, 20])
+    with pytest.raises(KeyError):
+        allocator.append_many([RequestId("a"), RequestId("zz")], key, value, [20, 20])
+    with pytest.raises(ValueError, match="sum"):
+        allocator.append_many([RequestId("a"), RequestId("b")], key, value, [20, 10])
+    assert allocator.capacity() == counts
+    assert torch.isnan(allocator.pool).all()
+    allocator.append_many([RequestId("a"), RequestId("b")], key[:, :30], value[:, :30], [20, 10])
+    assert allocator.cached_length(RequestId("a")) == 20 and allocator.cached_length(RequestId("b")) == 10
+
+
 def test_per_row_and_batched_decode_writes_agree(rope_golden: np.ndarray) -> None:
     device = cuda_device()
     lengths = [1, 15, 16, 17, 31, 32, 100]

@@ -178,6 +178,69 @@ def test_plan_does_not_mutate_and_commit_publishes(validation: str) -> None:
     assert slots.tolist() == list(range(16)) + list(range(16, 20))
 
 
+def churned_ledger(validation: str) -> BlockLedger:
+    """A ledger with a fragmented free list and three reserved, partly filled requests."""
+    ledger = BlockLedger(64, validation)
+    for request in range(10, 20):
+        ledger.reserve(request, 3)
+        ledger.append(request, 5 + request)
+    for request in (11, 14, 15, 18):
+        ledger.release(request)
+    for request, credits, filled in ((1, 8, 0), (2, 4, 20), (3, 6, 7)):
+        ledger.reserve(request, credits)
+        if filled:
+            ledger.append(request, filled)
+    return ledger
+
+
+def test_batched_append_takes_the_slots_of_sequential_appends(validation: str) -> None:
+    batched, sequential = churned_ledger(validation), churned_ledger(validation)
+    requests, tokens = [3, 1, 2], [40, 100, 13]
+    slots, starts = batched.append_plan_many(requests, tokens)
+    assert batched.capacity() == sequential.capacity()  # planning changes nothing
+    expected = [sequential.append(r, t) for r, t in zip(requests, tokens, strict=True)]
+    assert slots.tolist() == np.concatenate(expected).tolist()
+    assert starts.tolist() == [7, 0, 20]
+    batched.append_commit_many(requests, tokens)
+    assert batched.capacity() == sequential.capacity()
+    assert batched.free_list() == sequential.free_list()
+    for request in requests:
+        assert batched.table(request) == sequential.table(request)
+        assert batched.length(request) == sequential.length(request)
+
+
+@pytest.mark.parametrize(
+    "requests, tokens, error, match",
+    [
+        ([3, 2], [40, 60], RuntimeError, "exceeds request reservation"),  # the second overruns its credits
+        ([3, 2], [10, 2040], ValueError, "2048|invalid KV append"),  # 20 cached + 2040 > 2048
+        ([3, 99], [10, 1], KeyError, "99"),
+        ([3, 3], [1, 1], ValueError, "only once"),
+        ([3, 1], [10, 0], ValueError, "tokens|invalid KV append"),
+    ],
+)
+def test_a_failing_batched_append_changes_nothing(requests, tokens, error, match, validation: str) -> None:
+    ledger = churned_ledger(validation)
+    before = (ledger.capacity(), ledger.free_list(), [ledger.table(r) for r in (1, 2, 3)])
+    with pytest.raises(error, match=match):
+        ledger.append_plan_many(requests, tokens)
+    with pytest.raises(error, match=match):
+        ledger.append_commit_many(requests, tokens)
+    assert (ledger.capacity(), ledger.free_list(), [ledger.table(r) for r in (1, 2, 3)]) == before
+
+
+def test_batched_append_fills_the_pool_with_disjoint_slots(validation: str) -> None:
+    ledger = BlockLedger(6, validation)
+    for request in (1, 2):
+        ledger.reserve(request, 3)
+    ledger.append(1, 1)
+    slots, starts = ledger.append_plan_many([1, 2], [40, 48])
+    assert len(set(slots.tolist())) == 88 and starts.tolist() == [1, 0]
+    ledger.append_commit_many([1, 2], [40, 48])
+    assert ledger.length(1) == 41 and ledger.length(2) == 48
+    assert ledger.free_list() == [] and sorted(ledger.table(1) + ledger.table(2)) == list(range(6))
+
+
 def test_staged_decode_semantics(validation: str) -> None:
     # tests/unit/test_kv_cache.py:375-418
     ledger = BlockLedger(4, validation)
