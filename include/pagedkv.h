@@ -285,8 +285,8 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
  * and sets the kernel attributes with that device current; make that first
  * call before any stream capture.  All calls share the array and it keeps the
  * last call's contents (every partial is written before it is read within one
- * call; the slot-claim counters in it start at zero when the library loads
- * and every call leaves them at zero), so calls that overlap on the
+ * call; each call clears the slot-claim counters at its start on `stream`,
+ * without allocating), so calls that overlap on the
  * GPU - on different streams, or on one device from different threads - race
  * and must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
 int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,

@@ -1320,6 +1320,14 @@ extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks
     if (rc) return rc;
     CUtensorMap map;
     if ((rc = noalloc_pool_map(pool, num_blocks, &map))) return rc;
+    // The array keeps the last call's contents.  The slot-claim counters at its
+    // start must be zero when the split kernel starts; every completed call
+    // leaves them so, and this clear covers a call that did not complete.
+    e = cudaMemsetAsync(scratch, 0, 2 * kClaimWords * sizeof(int32_t), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        return pkv::fail(PKV_CUDA_ERROR, std::string("no-alloc decode attention: clearing the claim counters: ") +
+                                             cudaGetErrorString(e));
+    }
     return launch_pass<false>(grid, map, args, row_pieces, static_cast<cudaStream_t>(stream),
                               "no-alloc decode attention");
 }
