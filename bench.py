@@ -804,8 +804,8 @@ def run_append_arm(args: argparse.Namespace) -> None:
                 "algorithmic_bytes_per_step": step_bytes,
                 "avg_launch_ms": kernel_ms,
                 "traffic": None,
-                "traffic_note": "ncu reads per step = 1.007 x the K/V input (read once); the pool writes stay in L2 "
-                                "within a launch, so per-launch DRAM write counts undercount them "
+                "traffic_note": "ncu per launch: reads 1.004 x the K/V input (read once), writes 103-108 of the "
+                                "152 MB written (the rest still dirty in L2 at the launch's end) "
                                 "(profiles/append_kv_cfg2a.md)",
             },
             "e2e": {
