@@ -131,7 +131,7 @@ class DecodeStepGraph:
             graph = self._graphs.get(cache_key)
             if graph is None:
                 if len(self._graphs) >= self.max_graphs:
-                    self._graphs.clear()
+                    del self._graphs[next(iter(self._graphs))]  # the oldest capture
                 graph = self._graphs[cache_key] = self._capture(args, query, key, value, out)
             ledger = allocator._ledger
             ledger.decode_check(-1, 0)  # a fresh staged step: layer 0 is next
@@ -148,8 +148,9 @@ class DecoderStepGraph:
     the fused Q/K/V and gate/up GEMMs, the decode layer's split and combine,
     the output and down projections, the SwiGLU product) plus the embedding,
     the final norm and the logits: about 200 launches whose Python and launch
-    costs exceed the GPU time at small batches.  Here the whole step, ``BatchedDecoder.forward`` with the fused
-    decode layer launched on the step's padded tables, is captured once per
+    costs exceed the GPU time at small batches.  Here the whole step,
+    ``BatchedDecoder.forward`` with the fused decode layer launched on the
+    step's padded tables, is captured once per
     upload buffer and replayed: the host stages the step (ledger, tables, one
     upload), copies the token ids into a fixed buffer and launches the graph.
     ``step(input_ids, request_ids)`` returns the logits [B, 1, V] of
@@ -224,7 +225,7 @@ class DecoderStepGraph:
             entry = self._graphs.get(args)
             if entry is None:
                 if len(self._graphs) >= self.max_graphs:
-                    self._graphs.clear()
+                    del self._graphs[next(iter(self._graphs))]  # the oldest capture
                 entry = self._graphs[args] = self._capture(args)
             graph, logits = entry
             self.ids[:count].copy_(input_ids)
