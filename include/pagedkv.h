@@ -315,6 +315,14 @@ int pkv_add_rms_norm(void *hidden, const void *delta, const void *weight, void *
  * [rows][2 * inter], out [rows][inter]. */
 int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, void *stream);
 
+/* A linear layer (F.linear, dense.py's projections) for 1 to 8 rows:
+ * y[m][n] = fp16(sum_k x[m][k] * w[n][k]), the FP32 sum rounded once.  x
+ * [rows][k] with rows x_stride elements apart, w [n][k] contiguous, y rows
+ * y_stride elements apart; k a multiple of 8, x and w 16-byte aligned.  At
+ * decode batches of a few rows the layer is bound by reading w once. */
+int pkv_gemv(const void *x, int64_t x_stride, const void *w, int32_t rows, int32_t n, int32_t k, void *y,
+             int64_t y_stride, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

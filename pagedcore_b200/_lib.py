@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_rope_table_bytes": (c_int64, []),
     "pkv_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
     "pkv_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
+    "pkv_gemv": (c_int, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]),
     "pkv_append_kv": (
         c_int,
         [

@@ -153,3 +153,112 @@ extern "C" int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_
     if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(err));
     return PKV_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Small-batch linear layer: y[m][n] = fp16(sum_k x[m][k] * w[n][k]) for M <= 8
+// rows of x, the FP32 sum rounded once (as F.linear's FP16 GEMM, in another
+// summation order).  At decode batches of a few rows a linear layer is a
+// matrix-vector product bound by reading W once; this kernel streams W at
+// HBM speed where the library GEMM's small-M tiles do not.  One warp per row
+// of W: lane j reads 16-byte chunks j, j + 32, ... of the row, with up to 8
+// chunks in flight, and x (a few KB, L1-resident) alongside.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvUnroll = 8;
+
+__device__ __forceinline__ float dot8(const uint4 &a, const uint4 &b) {
+    const __half2 *ah = reinterpret_cast<const __half2 *>(&a);
+    const __half2 *bh = reinterpret_cast<const __half2 *>(&b);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 af = __half22float2(ah[i]);
+        const float2 bf = __half22float2(bh[i]);
+        sum = fmaf(af.x, bf.x, sum);
+        sum = fmaf(af.y, bf.y, sum);
+    }
+    return sum;
+}
+
+template <int M>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __half *__restrict__ x, int64_t x_stride,
+                                                               const __half *__restrict__ w, int n_rows, int k,
+                                                               __half *__restrict__ y, int64_t y_stride) {
+    const int lane = threadIdx.x & 31;
+    const int chunks = k / kChunk;
+    for (int n = blockIdx.x * kGemvWarps + (threadIdx.x >> 5); n < n_rows; n += gridDim.x * kGemvWarps) {
+        const __half *row = w + static_cast<int64_t>(n) * k;
+        float acc[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = 0.f;
+        for (int c0 = lane; c0 < chunks; c0 += 32 * kGemvUnroll) {
+            uint4 wv[kGemvUnroll];
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < chunks) wv[u] = *reinterpret_cast<const uint4 *>(row + c * kChunk);
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < chunks) {
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        const uint4 xv = *reinterpret_cast<const uint4 *>(x + m * x_stride + c * kChunk);
+                        acc[m] += dot8(wv[u], xv);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+#pragma unroll
+            for (int offset = 16; offset > 0; offset >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], offset);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) y[m * y_stride + n] = __float2half_rn(acc[m]);
+        }
+    }
+}
+
+template <int M>
+cudaError_t launch_gemv(const __half *x, int64_t x_stride, const __half *w, int n, int k, __half *y,
+                        int64_t y_stride, cudaStream_t stream) {
+    const int grid = (n + kGemvWarps - 1) / kGemvWarps;
+    gemv_kernel<M><<<grid, kGemvWarps * 32, 0, stream>>>(x, x_stride, w, n, k, y, y_stride);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int pkv_gemv(const void *x, int64_t x_stride, const void *w, int32_t rows, int32_t n, int32_t k, void *y,
+                        int64_t y_stride, void *stream) {
+    pkv::clear_error();
+    if (x == nullptr || w == nullptr || y == nullptr) return pkv::fail(PKV_VALUE_ERROR, "gemv: x, w and y are required");
+    if (rows < 1 || rows > 8 || n < 1 || k < kChunk || k % kChunk) {
+        return pkv::fail(PKV_VALUE_ERROR, "gemv: 1 to 8 rows of x, k a multiple of 8");
+    }
+    if (!aligned16(x) || !aligned16(w) || x_stride % kChunk || y_stride < n) {
+        return pkv::fail(PKV_VALUE_ERROR, "gemv: x and w must be 16-byte aligned with row strides in multiples of 8");
+    }
+    const auto *xh = static_cast<const __half *>(x);
+    const auto *wh = static_cast<const __half *>(w);
+    auto *yh = static_cast<__half *>(y);
+    const auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaSuccess;
+    switch (rows) {
+        case 1: err = launch_gemv<1>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 2: err = launch_gemv<2>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 3: err = launch_gemv<3>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 4: err = launch_gemv<4>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 5: err = launch_gemv<5>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 6: err = launch_gemv<6>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        case 7: err = launch_gemv<7>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+        default: err = launch_gemv<8>(xh, x_stride, wh, n, k, yh, y_stride, s); break;
+    }
+    if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("gemv launch failed: ") + cudaGetErrorString(err));
+    return PKV_OK;
+}

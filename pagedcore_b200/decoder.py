@@ -196,6 +196,8 @@ class BatchedDecoder:
         the residual add before it in the same kernel (``kernels.add_rms_norm``)
         and SwiGLU's product is one kernel (``kernels.silu_mul``), with the
         rounding points of the reference's eager ops (dense.py:17-21, 84-91).
+        Projections of a single row use this library's matrix-vector kernel
+        (``kernels.linear``), larger batches the library GEMM.
         """
         weights = self.weights
         batch = input_ids.shape[0]
@@ -203,19 +205,20 @@ class BatchedDecoder:
         hidden = F.embedding(input_ids, weights.embedding).view(batch, HIDDEN)  # updated in place
         x = torch.empty_like(hidden)
         delta = None  # the output still to be added to the residual stream
+        linear = kernels.linear  # the matrix-vector kernel for one row, the library GEMM above
         for index, layer in enumerate(weights.layers):
             kernels.add_rms_norm(hidden, delta, layer.input_norm, x)
-            qkv = F.linear(x, self.qkv[index])
+            qkv = linear(x, self.qkv[index])
             query = qkv[:, :q_width].view(batch, QUERY_HEADS, HEAD_DIM)
             key = qkv[:, q_width : q_width + kv_width].view(batch, KV_HEADS, HEAD_DIM)
             value = qkv[:, q_width + kv_width :].view(batch, KV_HEADS, HEAD_DIM)
             # RoPE(Q, K) + new-token KV write + attention: one fused launch.
             attention = attend(index, query, key, value)
-            delta = F.linear(attention.view(batch, HIDDEN), layer.o_proj)
+            delta = linear(attention.view(batch, HIDDEN), layer.o_proj)
             kernels.add_rms_norm(hidden, delta, layer.post_attention_norm, x)
-            delta = F.linear(kernels.silu_mul(F.linear(x, self.gate_up[index])), layer.down_proj)
+            delta = linear(kernels.silu_mul(linear(x, self.gate_up[index])), layer.down_proj)
         kernels.add_rms_norm(hidden, delta, weights.final_norm, x)
-        return F.linear(x, weights.lm_head).view(batch, 1, -1)
+        return linear(x, weights.lm_head).view(batch, 1, -1)
 
     @torch.inference_mode()
     def step(self, input_ids: Tensor, allocator: KVAllocator, request_ids: tuple[RequestId, ...]) -> Tensor:

@@ -366,3 +366,44 @@ def silu_mul(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
         out = torch.empty((rows, width // 2), dtype=torch.float16, device=gate_up.device)
     check(lib.pkv_silu_mul(_ptr(gate_up), _ptr(out), rows, width // 2, _stream(gate_up.device)))
     return out
+
+
+# Rows up to which ``linear`` uses the matrix-vector kernel.  Measured on
+# B200 against the library GEMM: at one row it is faster on the decoder's
+# small projections (3.5-7 us against 7-15 us) and equal on the 131 MB LM head
+# (5.5 TB/s both); from two rows on, each weight chunk reloads every row of x
+# from L1, and it falls behind on the large projections.
+GEMV_MAX_ROWS = 1
+
+
+def linear(x: Tensor, weight: Tensor, out: Tensor | None = None) -> Tensor:
+    """``F.linear(x, weight)`` for FP16 x [rows, k] and weight [n, k], no bias.
+
+    Up to ``GEMV_MAX_ROWS`` rows run this library's matrix-vector kernel
+    (``pkv_gemv``, bound by reading the weight once); more rows, or shapes it
+    does not take (k not a multiple of 8, unaligned or strided operands), run
+    the library GEMM.  Both sum in FP32 and round once, in different orders.
+    """
+    rows, k = x.shape
+    n = weight.shape[0]
+    if (
+        rows > GEMV_MAX_ROWS
+        or k % 8
+        or x.dtype != torch.float16
+        or weight.dtype != torch.float16
+        or weight.shape != (n, k)
+        or not weight.is_contiguous()
+        or x.stride(1) != 1
+        or x.stride(0) % 8
+        or x.data_ptr() % 16
+        or weight.data_ptr() % 16
+    ):
+        result = torch.nn.functional.linear(x, weight)
+        if out is None:
+            return result
+        out.copy_(result)
+        return out
+    if out is None:
+        out = torch.empty((rows, n), dtype=torch.float16, device=x.device)
+    check(lib.pkv_gemv(_ptr(x), x.stride(0), _ptr(weight), rows, n, k, _ptr(out), out.stride(0), _stream(x.device)))
+    return out

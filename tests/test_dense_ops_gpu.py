@@ -66,3 +66,50 @@ def test_fused_ops_reject_bad_shapes() -> None:
         kernels.add_rms_norm(hidden, None, torch.zeros(1024, dtype=torch.float16, device=device), hidden.clone())
     with pytest.raises(ValueError, match="gate_up"):
         kernels.silu_mul(torch.zeros(2, 7, dtype=torch.float16, device=device))
+
+
+def gemv(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor) -> None:
+    """pkv_gemv through the C ABI, whatever kernels.linear would dispatch."""
+    from pagedcore_b200._lib import check, lib
+
+    check(lib.pkv_gemv(x.data_ptr(), x.stride(0), weight.data_ptr(), x.shape[0], weight.shape[0], x.shape[1],
+                       out.data_ptr(), out.stride(0), torch.cuda.current_stream().cuda_stream))
+
+
+def sums_close(actual: torch.Tensor, expected: torch.Tensor) -> None:
+    """Same FP32 products summed in another order, each rounded once to FP16:
+    within 4 FP16 ulps (or 1e-5 near zero, where the sign may flip), and equal
+    for nearly all elements."""
+    torch.testing.assert_close(actual.float(), expected.float(), atol=1e-5, rtol=4 * 2.0**-10)
+    assert float((actual == expected).float().mean()) > 0.99
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("n, k", [(2560, 2048), (2048, 5632), (31, 2048), (32000, 2048)])
+def test_gemv_matches_the_fp32_product_rounded_once(rows, n, k) -> None:
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(rows * 7 + n)
+    x = torch.randn(rows, k, dtype=torch.float16, device=device, generator=generator)
+    weight = (0.02 * torch.randn(n, k, device=device, generator=generator)).half()
+    expected = (x.float() @ weight.float().T).half()
+    actual = torch.empty(rows, n, dtype=torch.float16, device=device)
+    gemv(x, weight, actual)  # the kernel itself, for every row count it takes
+    sums_close(actual, expected)
+    torch.testing.assert_close(actual, torch.nn.functional.linear(x, weight), atol=2e-3, rtol=2e-3)
+
+
+def test_gemv_takes_strided_rows_and_leaves_other_shapes_to_the_library() -> None:
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(3)
+    wide = torch.randn(4, 2560, dtype=torch.float16, device=device, generator=generator)
+    x = wide[:, 512:]  # rows 2560 elements apart
+    weight = (0.02 * torch.randn(96, 2048, device=device, generator=generator)).half()
+    actual = torch.empty(4, 96, dtype=torch.float16, device=device)
+    gemv(x, weight, actual)
+    sums_close(actual, (x.float() @ weight.float().T).half())
+    one = x[:1]
+    sums_close(kernels.linear(one, weight), (one.float() @ weight.float().T).half())  # one row: the kernel
+    many = torch.randn(9, 2048, dtype=torch.float16, device=device, generator=generator)  # the library GEMM
+    assert torch.equal(kernels.linear(many, weight), torch.nn.functional.linear(many, weight))
+    with pytest.raises(ValueError, match="1 to 8 rows"):
+        gemv(many, weight, torch.empty(9, 96, dtype=torch.float16, device=device))
