@@ -369,10 +369,11 @@ def silu_mul(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
 
 
 # Rows up to which ``linear`` uses the matrix-vector kernel.  Measured on
-# B200 against the library GEMM: at one row it is faster on the decoder's
-# small projections (3.5-7 us against 7-15 us) and equal on the 131 MB LM head
-# (5.5 TB/s both); from two rows on, each weight chunk reloads every row of x
-# from L1, and it falls behind on the large projections.
+# B200 against the library GEMM, weights read from DRAM: at one row it takes
+# 4.6-9.2 us against 7.4-17.3 us on the decoder's Q/K/V, output and down
+# projections, about the same on gate/up and the LM head; from two rows on the
+# library's tensor cores keep its time flat while this kernel turns CUDA-core
+# bound.
 GEMV_MAX_ROWS = 1
 
 
