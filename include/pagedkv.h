@@ -273,6 +273,23 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
                      int32_t blocks_per_cta, int32_t big_ctas, int32_t tail_blocks, void *out, int64_t out_stride,
                      void *workspace, int64_t workspace_bytes, int32_t *error_flag, int32_t flags, void *stream);
 
+/* Causal attention of a prompt chunk through its block table: the attention
+ * step of the prefill (dense_attention, dense.py:69-82, with decoder.py:225's
+ * mask) computed from the pool with paged_attention's numerics
+ * (attention.py:14-53: FP32 from FP16 pages, one FP16 rounding).  The chunk's
+ * `tokens` tokens sit at positions start .. start+tokens-1 of one request, and
+ * their K/V at `layer` are already in the pool (pkv_append_kv); token t attends
+ * to positions 0 .. start+t.  blocks: int32 device array, the physical block of
+ * each of the ceil((start+tokens)/16) blocks of the request (its block table);
+ * slots at or past start+tokens are never read.  query: rotated FP16
+ * [tokens][32][64], rows query_stride elements apart; out likewise with
+ * out_stride.  start + tokens <= 2048.  Allocates nothing, no workspace; one
+ * launch of ceil(tokens/16) x 4 CTAs.  Block ids outside [0, num_blocks) set
+ * PKV_DEVICE_BAD_BLOCK and read as zeros. */
+int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                          int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens, void *out,
+                          int64_t out_stride, int32_t *error_flag, void *stream);
+
 /* pkv_decode_attention without any allocation.  No counterpart in the
  * reference: it is for callers that cannot allocate device memory for this
  * library (a host whose device memory is all owned by another allocator, or a

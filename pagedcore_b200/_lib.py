@@ -180,6 +180,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
             c_void_p,  # stream
         ],
     ),
+    "pkv_prefill_attention": (
+        c_int,
+        [
+            c_void_p,  # pool
+            c_int32,  # num_blocks
+            c_int32,  # layer
+            c_void_p,  # query
+            c_int64,  # query_stride
+            c_void_p,  # blocks
+            c_int32,  # start
+            c_int32,  # tokens
+            c_void_p,  # out
+            c_int64,  # out_stride
+            c_void_p,  # error_flag
+            c_void_p,  # stream
+        ],
+    ),
 }
 
 

@@ -1,0 +1,310 @@
+// Causal prompt (prefill) attention through the block table, GQA, sm_100a.
+//
+// The attention of a prompt chunk whose K/V already sit in the pool: token t
+// of the chunk (position start + t) attends to positions 0 .. start + t of
+// its request, over the 16-token blocks its block table lists.  It stands in
+// for the causal attention of PagedCore's dense prefill (dense_attention,
+// src/pagedcore/dense.py:69-82, with the mask of decoder.py:225) with
+// the numerics of its paged attention (attention.py:14-53: FP32 scores,
+// softmax and sum from FP16 pages, one FP16 rounding of the output):
+//   out[t,h] = sum_{p <= start+t} softmax_p(q[t,h] . K[p, h/8] * 0.125) V[p, h/8]
+//
+// Work split - one CTA per (16-token query tile, KV head): 8 warps, warp w
+// holding tokens 2w and 2w+1 of the tile with the 8 query heads of the KV
+// head as the 16 rows of its MMA tiles (row r: token 2w + r/8, head r%8).
+// The CTA streams the blocks 0 .. (its last position)/16 once, so every K/V
+// block is read once per 128 query rows (the one-token decode kernel reads
+// it once per 8).  Tiles are taken longest first (the last tile of the chunk
+// has the most blocks), so the short ones fill in behind the long ones.
+//
+// Data movement - the 256 threads each copy one 16-byte chunk of the block's
+// 16 K rows or 16 V rows of this head (cp.async.cg, L2 only: the block is
+// read again by the chunk's other tiles) into shared memory with the 128-byte
+// XOR swizzle (chunk c of row r at c ^ (r & 7)), so the ldmatrix reads are
+// bank-conflict free, through a STAGES-deep ring of (K, V) tiles.  Slots at
+// or past start + tokens (not written yet; they may hold anything) are
+// zero-filled by the copy itself, so 0 * NaN never reaches the PV sum.  No
+// wait in this kernel polls a flag: cp.async.wait_group and __syncthreads
+// complete when the issued copies complete.
+//
+// Math - mma.sync m16n8k16, FP16 in, FP32 accumulate:
+//   S[16 rows x 16 keys]  = Q[16 x 64] . K^T[64 x 16]     (8 MMAs)
+//   O[16 rows x 64 dims] += P[16 x 16] . V[16 x 64]       (8 MMAs)
+// The S accumulator is the P operand in place (the m16n8 C layout of two
+// adjacent key tiles is the m16k16 A layout).  Online softmax in base 2 with
+// FP32 state; P is rounded to FP16 after scaling by 2^15, and the normaliser
+// sums the same rounded weights, as in the decode kernel.
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "pagedkv.h"
+#include "ptx.cuh"
+#include "status.h"
+
+namespace {
+
+constexpr int kHeadDim = PKV_HEAD_DIM;
+constexpr int kKvHeads = PKV_KV_HEADS;
+constexpr int kQueryHeads = PKV_QUERY_HEADS;
+constexpr int kGroup = kQueryHeads / kKvHeads;  // 8 query heads per KV head
+constexpr int kBlockTokens = PKV_BLOCK_TOKENS;
+constexpr int kRowBytes = kHeadDim * 2;              // 128 B: one head of one token
+constexpr int kTileBytes = kBlockTokens * kRowBytes; // 2 KiB: one head of one block
+constexpr int kStages = 4;
+constexpr int kTileTokens = 16;                      // query tokens per CTA
+constexpr int kWarps = kTileTokens / 2;              // 2 tokens x 8 heads = 16 MMA rows a warp
+constexpr int kThreads = kWarps * 32;
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
+constexpr float kWeightShift = 15.0f;                       // P scaled by 2^15 before FP16
+static_assert(kThreads == 2 * kBlockTokens * (kRowBytes / 16), "one 16-byte copy per thread per block");
+static_assert(kGroup == 8, "a KV head's query heads fill 8 MMA rows");
+
+struct PrefillArgs {
+    const __half *pool;
+    const __half *query;
+    __half *out;
+    const int32_t *blocks;  // physical block of each 16-position block of the request
+    int64_t query_stride;   // elements between tokens
+    int64_t out_stride;
+    int32_t num_blocks;
+    int32_t layer;
+    int32_t start;   // position of the chunk's first token
+    int32_t tokens;  // chunk tokens
+    int32_t *error_flag;
+};
+
+__device__ __forceinline__ float quad_max(float v) {
+    // The 4 lanes of a quad hold the 16 keys of one MMA row.
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
+__device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+__global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const PrefillArgs a) {
+    __shared__ __align__(128) uint8_t ring[kStages * 2 * kTileBytes];
+
+    const int tile = gridDim.x - 1 - blockIdx.x;  // longest tiles first
+    const int kv = blockIdx.y;
+    const int t0 = tile * kTileTokens;
+    const int last_token = min(t0 + kTileTokens - 1, a.tokens - 1);
+    const int blocks = (a.start + last_token) / kBlockTokens + 1;  // blocks 0 .. blocks-1
+    const int written = a.start + a.tokens;                         // positions below hold K/V
+
+    // This thread's copy: 16 bytes (chunk `ch`) of K or V row `key` of each block.
+    const int part = threadIdx.x >> 7;  // 0: K, 1: V
+    const int key = (threadIdx.x >> 3) & (kBlockTokens - 1);
+    const int ch = threadIdx.x & 7;
+    const uint32_t ring_base = pkv::smem_addr(ring);
+    const uint32_t copy_dst = ring_base + part * kTileBytes + key * kRowBytes + ((ch ^ (key & 7)) << 4);
+    const int64_t part_blocks = (static_cast<int64_t>(a.layer) * 2 + part) * a.num_blocks;
+    const __half *copy_src = a.pool + kv * kHeadDim + ch * 8;
+    auto issue = [&](int j) {
+        const int32_t block = a.blocks[j];
+        const bool ok = block >= 0 && block < a.num_blocks;
+        if (!ok && threadIdx.x == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
+        const __half *src =
+            copy_src + ((part_blocks + (ok ? block : 0)) * kBlockTokens + key) * (kKvHeads * kHeadDim);
+        const uint32_t bytes = ok && j * kBlockTokens + key < written ? 16u : 0u;
+        pkv::cp_async_16(copy_dst + (j % kStages) * (2 * kTileBytes), src, bytes);
+    };
+#pragma unroll
+    for (int j = 0; j < kStages - 1; ++j) {
+        if (j < blocks) issue(j);
+        pkv::cp_async_commit();
+    }
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const int token_a = t0 + 2 * warp;  // MMA rows g     (head g of the group)
+    const int token_b = token_a + 1;    // MMA rows g + 8
+    const int qa = min(token_a, a.tokens - 1);
+    const int qb = min(token_b, a.tokens - 1);
+    const int lim_a = a.start + qa;  // last position each row attends to
+    const int lim_b = a.start + qb;
+    const int warp_blocks = token_a < a.tokens ? lim_b / kBlockTokens + 1 : 0;
+    const int head = kv * kGroup + g;
+
+    // Q as the A operand: (row g | g+8, dims 16ks + 2t, +1 | +8, +9).
+    uint32_t qf[4][4];
+    {
+        const __half *qa_row = a.query + qa * a.query_stride + head * kHeadDim + 2 * t;
+        const __half *qb_row = a.query + qb * a.query_stride + head * kHeadDim + 2 * t;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            qf[ks][0] = ld32(qa_row + 16 * ks);
+            qf[ks][1] = ld32(qb_row + 16 * ks);
+            qf[ks][2] = ld32(qa_row + 16 * ks + 8);
+            qf[ks][3] = ld32(qb_row + 16 * ks + 8);
+        }
+    }
+
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+
+    for (int j = 0; j < blocks; ++j) {
+        // Block j's copies (group j) are complete; every warp is done with the
+        // stage the next copy overwrites (block j - 1's).
+        pkv::cp_async_wait<kStages - 2>();
+        __syncthreads();
+        if (j + kStages - 1 < blocks) issue(j + kStages - 1);
+        pkv::cp_async_commit();
+        if (j >= warp_blocks) continue;
+
+        const uint32_t ktile = ring_base + (j % kStages) * (2 * kTileBytes);
+        const uint32_t vtile = ktile + kTileBytes;
+        // kf[ks]: (keys 0-7 | 8-15) x (dims 16ks.. | 16ks+8..); vf[mt]: V^T of dims 16mt..16mt+15.
+        uint32_t kf[4][4], vf[4][4];
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            const int mat = lane >> 3;
+            const int tok = (lane & 7) + ((mat & 1) << 3);
+            const int chunk = 2 * ks + (mat >> 1);
+            pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), kf[ks][0], kf[ks][1], kf[ks][2],
+                             kf[ks][3]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            const int mat = lane >> 3;
+            const int tok = (lane & 7) + ((mat >> 1) << 3);
+            const int chunk = 2 * mt + (mat & 1);
+            pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), vf[mt][0], vf[mt][1],
+                                   vf[mt][2], vf[mt][3]);
+        }
+
+        // S = Q . K^T: s[nt] holds keys 8nt + 2t, +1 of rows g (0, 1) and g + 8 (2, 3).
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+            pkv::mma_f16_16816(s[0], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], kf[ks][0], kf[ks][2]);
+            pkv::mma_f16_16816(s[1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], kf[ks][1], kf[ks][3]);
+        }
+        const int p0 = j * kBlockTokens + 2 * t;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int pos = p0 + 8 * nt + e;
+                s[nt][e] = pos <= lim_a ? s[nt][e] * kScaleLog2 : -INFINITY;
+                s[nt][2 + e] = pos <= lim_b ? s[nt][2 + e] * kScaleLog2 : -INFINITY;
+            }
+        }
+        // Position 0 is in every row's range and block 0 comes first, so the
+        // running maxima are finite from the first block on.
+        const float mn_a = fmaxf(m_a, quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]))));
+        const float mn_b = fmaxf(m_b, quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]))));
+        const float alpha_a = pkv::exp2_approx(m_a - mn_a);
+        const float alpha_b = pkv::exp2_approx(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        __half2 p[2][2];  // p[nt][0]: row g, p[nt][1]: row g + 8 (keys 8nt + 2t, +1)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            p[nt][0] = __floats2half2_rn(pkv::exp2_approx(s[nt][0] - mn_a + kWeightShift),
+                                         pkv::exp2_approx(s[nt][1] - mn_a + kWeightShift));
+            p[nt][1] = __floats2half2_rn(pkv::exp2_approx(s[nt][2] - mn_b + kWeightShift),
+                                         pkv::exp2_approx(s[nt][3] - mn_b + kWeightShift));
+        }
+        const float2 fa0 = __half22float2(p[0][0]), fa1 = __half22float2(p[1][0]);
+        const float2 fb0 = __half22float2(p[0][1]), fb1 = __half22float2(p[1][1]);
+        l_a = l_a * alpha_a + ((fa0.x + fa0.y) + (fa1.x + fa1.y));
+        l_b = l_b * alpha_b + ((fb0.x + fb0.y) + (fb1.x + fb1.y));
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+            o[dt][0] *= alpha_a;
+            o[dt][1] *= alpha_a;
+            o[dt][2] *= alpha_b;
+            o[dt][3] *= alpha_b;
+        }
+        // O += P . V: P's A fragments are the S accumulators of key tiles 0 and 1.
+        const uint32_t a0 = pkv::pack_half2(p[0][0]), a1 = pkv::pack_half2(p[0][1]);
+        const uint32_t a2 = pkv::pack_half2(p[1][0]), a3 = pkv::pack_half2(p[1][1]);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+            pkv::mma_f16_16816(o[2 * mt], a0, a1, a2, a3, vf[mt][0], vf[mt][2]);
+            pkv::mma_f16_16816(o[2 * mt + 1], a0, a1, a2, a3, vf[mt][1], vf[mt][3]);
+        }
+    }
+    pkv::cp_async_wait<0>();
+
+    l_a = quad_sum(l_a);
+    l_b = quad_sum(l_b);
+    if (token_a < a.tokens) {
+        __half *dst = a.out + token_a * a.out_stride + head * kHeadDim + 2 * t;
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+            *reinterpret_cast<__half2 *>(dst + 8 * dt) =
+                __floats2half2_rn(__fdiv_rn(o[dt][0], l_a), __fdiv_rn(o[dt][1], l_a));
+        }
+    }
+    if (token_b < a.tokens) {
+        __half *dst = a.out + token_b * a.out_stride + head * kHeadDim + 2 * t;
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+            *reinterpret_cast<__half2 *>(dst + 8 * dt) =
+                __floats2half2_rn(__fdiv_rn(o[dt][2], l_b), __fdiv_rn(o[dt][3], l_b));
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                     int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens,
+                                     void *out, int64_t out_stride, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    if (pool == nullptr || query == nullptr || blocks == nullptr || out == nullptr || error_flag == nullptr) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: null pointer argument");
+    }
+    if (layer < 0 || layer >= PKV_LAYERS) {
+        return pkv::fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
+    }
+    if (num_blocks < 1 || static_cast<int64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens > INT32_MAX) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: pool block count out of range");
+    }
+    if (tokens < 1 || start < 0 || static_cast<int64_t>(start) + tokens > PKV_CONTEXT_LIMIT) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: the chunk must hold 1 or more tokens at positions below 2048");
+    }
+    const int64_t row = static_cast<int64_t>(kQueryHeads) * kHeadDim;
+    if ((reinterpret_cast<uintptr_t>(pool) & 15) || (reinterpret_cast<uintptr_t>(query) & 3) ||
+        (reinterpret_cast<uintptr_t>(out) & 3) || (reinterpret_cast<uintptr_t>(blocks) & 3) || query_stride % 2 ||
+        out_stride % 2 || query_stride < row || out_stride < row) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: misaligned tensor");
+    }
+    PrefillArgs args;
+    args.pool = static_cast<const __half *>(pool);
+    args.query = static_cast<const __half *>(query);
+    args.out = static_cast<__half *>(out);
+    args.blocks = blocks;
+    args.query_stride = query_stride;
+    args.out_stride = out_stride;
+    args.num_blocks = num_blocks;
+    args.layer = layer;
+    args.start = start;
+    args.tokens = tokens;
+    args.error_flag = error_flag;
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3((tokens + kTileTokens - 1) / kTileTokens, kKvHeads);
+    config.blockDim = dim3(kThreads);
+    config.dynamicSmemBytes = 0;
+    config.stream = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = cudaLaunchKernelEx(&config, prefill_attention_kernel, args);
+    if (e != cudaSuccess) {
+        return pkv::fail(PKV_CUDA_ERROR, std::string("prefill attention launch failed: ") + cudaGetErrorString(e));
+    }
+    return PKV_OK;
+}

@@ -144,4 +144,19 @@ __device__ __forceinline__ uint32_t pack_half2(__half2 h) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// 16-byte asynchronous global -> shared copy through L2 (cp.async.cg); only
+// `src_bytes` (0 or 16) are read, the rest of the 16 bytes are zero-filled.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Wait until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace pkv

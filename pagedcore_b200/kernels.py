@@ -270,6 +270,36 @@ def decode_attention(
     return out
 
 
+def prefill_attention(
+    pool: Tensor, layer: int, query: Tensor, blocks: Tensor, start: int, out: Tensor, error_flag: Tensor
+) -> Tensor:
+    """Causal attention of a prompt chunk's rotated FP16 query [T, 32, 64] into ``out``.
+
+    Token t of the chunk sits at position ``start + t`` and attends to
+    positions 0 .. start + t through ``blocks`` (int32, the request's physical
+    block per 16 positions); the chunk's K/V must already be in the pool.
+    """
+    device = pool.device
+    if query.ndim != 3 or query.shape[1:] != (_QUERY_HEADS, _HEAD_DIM) or query.dtype != torch.float16:
+        raise ValueError("query must be FP16 [tokens, 32, 64]")
+    if query.stride()[1:] != (_HEAD_DIM, 1):
+        query = query.contiguous()
+    if out.shape != query.shape or out.dtype != torch.float16 or out.stride()[1:] != (_HEAD_DIM, 1):
+        raise ValueError("out must be FP16 [tokens, 32, 64] with contiguous rows")
+    tokens = query.shape[0]
+    if blocks.dtype != torch.int32 or blocks.ndim != 1 or blocks.numel() * 16 < start + tokens:
+        raise ValueError("blocks must be int32 with one entry per 16 positions of the chunk's request")
+    for name, tensor in (("query", query), ("out", out), ("blocks", blocks)):
+        _require_cuda(name, tensor, device)
+    check(
+        lib.pkv_prefill_attention(
+            _ptr(pool), pool.shape[2], layer, _ptr(query), query.stride(0), _ptr(blocks), start, tokens,
+            _ptr(out), out.stride(0), _ptr(error_flag), _stream(device),
+        )
+    )
+    return out
+
+
 def decode_layer(
     pool: Tensor,
     layer: int,

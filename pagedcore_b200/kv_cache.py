@@ -175,13 +175,16 @@ class _StepUploads:
 class PrefillAppend:
     """One planned prompt chunk of ``KVAllocator.prefill_append``."""
 
-    def __init__(self, allocator: KVAllocator, batch: DecodeBatch, slots: Tensor, positions: Tensor,
-                 tokens: int) -> None:
+    def __init__(self, allocator: KVAllocator, blocks: np.ndarray, device_blocks: Tensor, slots: Tensor,
+                 positions: Tensor, start: int, tokens: int) -> None:
         self._allocator = allocator
-        self.batch = batch
+        self._host_blocks = blocks
+        self.blocks = device_blocks
         self.slots = slots
         self.positions = positions
+        self.start = start
         self.tokens = tokens
+        self._split_batch: DecodeBatch | None = None
 
     @torch.inference_mode()
     def write_layer(self, layer: int, key: Tensor, value: Tensor, query: Tensor) -> Tensor:
@@ -200,8 +203,25 @@ class PrefillAppend:
 
     @torch.inference_mode()
     def attend(self, layer: int, query: Tensor, out: Tensor | None = None) -> Tensor:
-        """Causal attention [T, 32, 64] of the rotated chunk queries at `layer` over the pool."""
-        return self._allocator.attend(self.batch, query, layer_index=layer, out=out)
+        """Causal attention [T, 32, 64] of the rotated chunk queries at `layer` over the pool.
+
+        One launch of the prefill kernel (``pkv_prefill_attention``): every
+        16-token query tile streams the request's blocks once.
+        """
+        allocator = self._allocator
+        allocator._check_worker()
+        if type(layer) is not int or not 0 <= layer < _LAYERS:
+            raise ValueError("layer_index must identify one of the 22 decoder layers")
+        if out is None:
+            out = torch.empty(query.shape, dtype=torch.float16, device=allocator._pool.device)
+        return kernels.prefill_attention(allocator._pool, layer, query, self.blocks, self.start, out, allocator._error)
+
+    @torch.inference_mode()
+    def attend_split(self, layer: int, query: Tensor, out: Tensor | None = None) -> Tensor:
+        """The same attention through the split-K decode kernel, token t as a row of length start + t + 1."""
+        if self._split_batch is None:
+            self._split_batch = self._allocator._prefill_batch(self._host_blocks, self.start, self.tokens)
+        return self._allocator.attend(self._split_batch, query, layer_index=layer, out=out)
 
 
 def padded_tables(
@@ -559,20 +579,11 @@ class KVAllocator:
              for j in range(-(-(start + tokens) // 16))],
             dtype=np.int32,
         )
-        # Token t of the chunk (position start + t) attends to positions 0..start+t.
-        lengths = np.arange(start + 1, start + tokens + 1, dtype=np.int32)
-        counts = -(-lengths // 16)
-        prefix = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
-        total = int(prefix[-1])
-        flat = blocks[np.arange(total) - np.repeat(prefix[:-1], counts)]
-        plan = kernels.decode_plan(self._pool.device, tokens, total)
-        pieces, row_pieces = kernels.decode_tables(prefix, plan.grid)
-        tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), lengths, prefix, flat))
         positions = np.arange(start, start + tokens, dtype=np.int32)
-        device = self._upload_i32(tables, slots, positions)
-        batch = self._device_batch((), tables, total, plan, device[: len(tables)], rows=tokens)
-        chunk = PrefillAppend(self, batch, device[len(tables) : len(tables) + tokens],
-                              device[len(tables) + tokens :], tokens)
+        device = self._upload_i32(blocks, slots, positions)
+        count = len(blocks)
+        chunk = PrefillAppend(self, blocks, device[:count], device[count : count + tokens],
+                              device[count + tokens :], start, tokens)
         yield chunk
         self._ledger.append_commit(handle, tokens)
 
@@ -908,6 +919,18 @@ class KVAllocator:
     def _upload_batch(self, request_ids: tuple[RequestId, ...], handles: np.ndarray, layer: int) -> DecodeBatch:
         tables, total, plan = self._batch_tables(request_ids, handles, layer)
         return self._device_batch(request_ids, tables, total, plan, self._upload_i32(tables))
+
+    def _prefill_batch(self, blocks: np.ndarray, start: int, tokens: int) -> DecodeBatch:
+        """A prompt chunk as a decode batch: token t is a row of length start + t + 1 over ``blocks``."""
+        lengths = np.arange(start + 1, start + tokens + 1, dtype=np.int32)
+        counts = -(-lengths // 16)
+        prefix = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+        total = int(prefix[-1])
+        flat = blocks[np.arange(total) - np.repeat(prefix[:-1], counts)]
+        plan = kernels.decode_plan(self._pool.device, tokens, total)
+        pieces, row_pieces = kernels.decode_tables(prefix, plan.grid)
+        tables = np.concatenate((pieces.reshape(-1), row_pieces.reshape(-1), lengths, prefix, flat))
+        return self._device_batch((), tables, total, plan, self._upload_i32(tables), rows=tokens)
 
     def attend(self, batch: DecodeBatch, query: Tensor, *, layer_index: int, out: Tensor | None = None) -> Tensor:
         """Decode attention of FP16 query [B, 32, 64] over a :class:`DecodeBatch`."""

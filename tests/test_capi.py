@@ -47,6 +47,9 @@ def test_device_entry_points_reject_bad_arguments_before_any_launch() -> None:
     )
     assert status == _lib.PKV_VALUE_ERROR
     assert b"null pointer" in _lib.lib.pkv_last_error()
+    status = _lib.lib.pkv_prefill_attention(None, 1, 0, None, 2048, None, 0, 1, None, 2048, None, None)
+    assert status == _lib.PKV_VALUE_ERROR
+    assert b"prefill attention: null pointer" in _lib.lib.pkv_last_error()
 
 
 def test_decode_entry_points_reject_a_partition_that_does_not_cover_the_blocks() -> None:
