@@ -39,6 +39,7 @@ SEQUENCES = 256  # per GPU (config 4); --sequences overrides it for small profil
 LAYERS = 22
 CALIBRATION_STEPS = 8  # staged steps in which KVAllocator(balance="measured") learns its piece weights
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TENSOR_TFLOPS = 1590.0
 
 
 # ---------------------------------------------------------------------------
@@ -176,6 +177,17 @@ def _peak_hbm() -> tuple[float, str]:
         except (KeyError, ValueError):
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def _peak_tensor() -> tuple[float, str]:
+    """Dense FP16/BF16 tensor peak in TFLOP/s (the burst figure: the kernel is timed alone)."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["bf16_tflops"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_TENSOR_TFLOPS, "fallback"
 
 
 def _traffic_ratio() -> float | None:
@@ -971,6 +983,163 @@ def run_decoder_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def run_prefill_arm(args: argparse.Namespace) -> None:
+    """Row f2: a whole prompt prefilled through the pool (``BatchedDecoder.prefill``).
+
+    Random-init TinyLlama weights, one prompt of ``--prompt`` tokens (default
+    2047, the longest that leaves room for a generated token) per GPU and step,
+    into an empty request: embedding, 22 x (norm, fused Q/K/V GEMM, K/V write
+    with RoPE, causal prefill attention over the block table, output
+    projection, norm, gate/up GEMM, SwiGLU product, down projection), final
+    norm and LM head for every prompt token.  The roofline is the hand-written
+    attention kernel's (``prefill_attention_kernel``), timed alone over the
+    same chunk on the same stream: its algorithmic MMA work over the measured
+    dense tensor peak.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from pagedcore_b200.decoder import BatchedDecoder
+    from pagedcore_b200.engine_types import KVReservation, RequestId
+    from pagedcore_b200.kv_cache import KVAllocator
+    from pagedcore_b200.weights import random_weights
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    host_affinity = _bind_host_cores(local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    seed = 6 + 1000 * rank
+    tokens = args.prompt
+    if not 1 <= tokens <= 2047:
+        raise SystemExit("--prompt must lie in [1, 2047]")
+    blocks = -(-tokens // 16)
+    pool = torch.empty((LAYERS, 2, blocks + 8, 16, 4, 64), dtype=torch.float16, device=device)
+    allocator = KVAllocator(pool, validation="incremental")
+    weights = random_weights(seed, device)
+    decoder = BatchedDecoder(weights)
+    generator = torch.Generator(device="cpu").manual_seed(seed)
+    host_ids = torch.randint(0, 32000, (1, tokens), generator=generator).pin_memory()
+    ids = host_ids.to(device)
+    request = RequestId("prompt")
+    stream = torch.cuda.current_stream(device)
+
+    def prefill(prompt):
+        allocator.create(KVReservation(request, blocks))
+        logits = decoder.prefill(prompt, allocator, request)
+        allocator.release_all(request)
+        return logits
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        prefill(ids)
+    torch.cuda.synchronize(device)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            logits = prefill(ids)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    step_ms = start.elapsed_time(end) / args.steps
+    # End to end through the public call: the prompt ids copied from pinned
+    # host memory and the last token's logits read back, every step.
+    last = torch.empty((1, 32000), dtype=torch.float16, pin_memory=True)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_start.record(stream)
+    for _ in range(args.steps):
+        prompt = host_ids.to(device, non_blocking=True)
+        last.copy_(prefill(prompt)[0, -1:], non_blocking=True)
+    e2e_end.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
+    # The attention kernel alone, one layer of the same chunk, on the same stream.
+    allocator.create(KVReservation(request, blocks))
+    query = torch.randn(tokens, 32, 64, dtype=torch.float16, device=device)
+    key = torch.randn(tokens, 4, 64, dtype=torch.float16, device=device)
+    with allocator.prefill_append(request, tokens) as chunk:
+        rotated = chunk.write_layer(0, key, key, query)
+        out = torch.empty_like(rotated)
+        for _ in range(3):
+            chunk.attend(0, rotated, out)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            chunk.attend(0, rotated, out)
+        b.record(stream)
+        torch.cuda.synchronize(device)
+    allocator.release_all(request)
+    attention_us = a.elapsed_time(b) / args.steps * 1000.0
+    allocator.check_device_errors()
+    times = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms = (float(x) for x in times.tolist())
+    if rank == 0:
+        peak, peak_kind = _peak_tensor()
+        # Token t attends to t + 1 positions: QK^T and PV are 2 x 2 x 64 FLOP
+        # per (query head, position) pair.
+        flops = 4.0 * 64 * 32 * tokens * (tokens + 1) / 2
+        achieved = flops / (attention_us * 1e-6) / 1e12
+        line = {
+            "metric": "prompt tokens/s, whole TinyLlama prefill through the pool (row f2: paged prefill)",
+            "value": world * tokens / (step_ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (random-init TinyLlama weights N(0, 0.02), random prompt token ids)",
+            "config": {
+                "workload": f"one {tokens}-token prompt per GPU per step into an empty request, every layer's K/V "
+                            "written to the pool and attended through the block table (BatchedDecoder.prefill); "
+                            "weights (2.2 GB) larger than L2",
+                "parallelism": f"dp{world} (independent prompts, weights replicated, no collective)",
+            },
+            "e2e": {
+                "value": world * tokens / (e2e_ms / 1000.0),
+                "unit": "tokens/s",
+                "h2d_bytes_per_step": tokens * 8,
+                "d2h_bytes_per_step": 32000 * 2,
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "prefill_attention_kernel (mma.sync m16n8k16, FP16 in, FP32 accumulate)",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "flops_per_launch": flops,
+                "launch_us": attention_us,
+                "traffic": None,
+            },
+            "gpu_launches_attention_per_step": LAYERS,
+            "logits_finite": bool(torch.isfinite(logits).all().item()),
+            "clocks": clocks.summary(),
+            "host_affinity": host_affinity,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -980,9 +1149,11 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
-    parser.add_argument("--workload", choices=("decode", "stress", "append", "decoder"), default="decode",
+    parser.add_argument("--workload", choices=("decode", "stress", "append", "decoder", "prefill"), default="decode",
                         help="decode: config 4 (the headline line); stress: config 5 (allocator churn); "
-                             "append: config 2a (prompt K/V appends); decoder: row f1 (whole decoder step)")
+                             "append: config 2a (prompt K/V appends); decoder: row f1 (whole decoder step); "
+                             "prefill: row f2 (a whole prompt through the pool)")
+    parser.add_argument("--prompt", type=int, default=2047, help="prompt tokens of the prefill workload")
     parser.add_argument("--stress-iterations", type=int, default=300)
     parser.add_argument("--stress-warmup", type=int, default=200)
     args = parser.parse_args()
@@ -997,6 +1168,8 @@ def main() -> None:
         run_append_arm(args)
     elif args.workload == "decoder":
         run_decoder_arm(args)
+    elif args.workload == "prefill":
+        run_prefill_arm(args)
     else:
         run_gpu_arm(args)
 

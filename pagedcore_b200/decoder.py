@@ -227,6 +227,28 @@ class BatchedDecoder:
         with allocator.append_decode(request_ids):
             return self.forward(input_ids, allocator.decode_layer)
 
+    @torch.inference_mode()
+    def prefill(self, input_ids: Tensor, allocator: KVAllocator, request_id: RequestId) -> Tensor:
+        """Prefill a prompt chunk [1, T] through the pool; return its logits [1, T, V].
+
+        ``prefill_paged_fused`` on the batched step's ops: the T prompt tokens
+        are the rows of ``forward`` (fused Q/K/V and gate/up GEMMs, fused
+        residual add + RMSNorm and SwiGLU product), and each layer's attention
+        writes the chunk's K (rotated) and V to its pool slots and runs the
+        causal prefill kernel over the block table.  The request may already
+        hold a cache (the chunk continues it); positions are published only
+        after the whole forward succeeds.
+        """
+        _check_prompt(input_ids, self.weights)
+        tokens = input_ids.shape[1]
+        with allocator.prefill_append(request_id, tokens) as chunk:
+
+            def attend(index: int, query: Tensor, key: Tensor, value: Tensor) -> Tensor:
+                return chunk.attend(index, chunk.write_layer(index, key, value, query))
+
+            logits = self.forward(input_ids.view(tokens, 1), attend)
+        return logits.view(1, tokens, -1)
+
 
 def decode_batched(
     input_ids: Tensor, weights: TinyLlamaWeights, allocator: KVAllocator, request_ids: tuple[RequestId, ...]

@@ -308,6 +308,33 @@ def test_fused_paged_prefill_matches_the_dense_prefill(small) -> None:
     fused.check_device_errors()
 
 
+def test_batched_prefill_matches_the_dense_prefill_and_continues_a_cache(small) -> None:
+    # BatchedDecoder.prefill: 49 prompt tokens as 20 + 29 must give the dense
+    # logits, leave the fused path's cache, and decode on from it.
+    device = cuda_device()
+    batched, fused = new_allocator(8, device), new_allocator(8, device)
+    request = RequestId("b")
+    for allocator in (batched, fused):
+        allocator.create(KVReservation(request, 4))
+    ids = small_prompt(49).to(device)
+    full, _ = prefill(ids, small)
+    model = BatchedDecoder(small)
+    first = model.prefill(ids[:, :20], batched, request)
+    second = model.prefill(ids[:, 20:], batched, request)
+    got = torch.cat((first, second), dim=1)
+    torch.testing.assert_close(got, full, atol=LOGIT_TOL, rtol=LOGIT_TOL)
+    assert torch.equal(got.argmax(-1), full.argmax(-1))
+    decoder.prefill_paged_fused(ids, small, fused, request)
+    assert batched.block_table(request) == fused.block_table(request) and batched.cached_length(request) == 49
+    table = batched.block_table(request)
+    for logical, physical in enumerate(table):
+        valid = min(16, 49 - 16 * logical)
+        # Same rounding points; the fused norm may sum the squares in another order.
+        torch.testing.assert_close(batched.pool[0, :, physical, :valid], fused.pool[0, :, physical, :valid],
+                                   atol=2e-3, rtol=1e-2)
+    batched.check_device_errors()
+
+
 def test_fused_paged_prefill_continues_a_cache_in_chunks(small) -> None:
     # Prompt of 49 tokens prefilled as 20 + 29 must give the dense logits of positions 20..48.
     device = cuda_device()
