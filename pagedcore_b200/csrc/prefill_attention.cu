@@ -15,13 +15,15 @@
 // The CTA streams the blocks 0 .. (its last position)/16 once, so every K/V
 // block is read once per 128 query rows (the one-token decode kernel reads
 // it once per 8).  Tiles are taken longest first (the last tile of the chunk
-// has the most blocks), so the short ones fill in behind the long ones.
+// has the most blocks) across all four heads, so the short ones fill in
+// behind the long ones.
 //
 // Data movement - the 256 threads each copy one 16-byte chunk of the block's
 // 16 K rows or 16 V rows of this head (cp.async.cg, L2 only: the block is
 // read again by the chunk's other tiles) into shared memory with the 128-byte
 // XOR swizzle (chunk c of row r at c ^ (r & 7)), so the ldmatrix reads are
-// bank-conflict free, through a STAGES-deep ring of (K, V) tiles.  Slots at
+// bank-conflict free, through a 4-deep ring of (K, V) tiles (8 deep measured
+// the same); the block ids are staged in shared memory once.  Slots at
 // or past start + tokens (not written yet; they may hold anything) are
 // zero-filled by the copy itself, so 0 * NaN never reaches the PV sum.  No
 // wait in this kernel polls a flag: cp.async.wait_group and __syncthreads
@@ -33,7 +35,10 @@
 // The S accumulator is the P operand in place (the m16n8 C layout of two
 // adjacent key tiles is the m16k16 A layout).  Online softmax in base 2 with
 // FP32 state; P is rounded to FP16 after scaling by 2^15, and the normaliser
-// sums the same rounded weights, as in the decode kernel.
+// sums the same rounded weights, as in the decode kernel.  Only the blocks
+// that cross a row's last position are masked, the scale is folded into the
+// exponent's FMA, and O and l are rescaled only when a row's maximum moves
+// (the factor would be exactly 1 otherwise).
 
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -56,6 +61,7 @@ constexpr int kBlockTokens = PKV_BLOCK_TOKENS;
 constexpr int kRowBytes = kHeadDim * 2;              // 128 B: one head of one token
 constexpr int kTileBytes = kBlockTokens * kRowBytes; // 2 KiB: one head of one block
 constexpr int kStages = 4;
+constexpr int kMaxTableBlocks = PKV_CONTEXT_LIMIT / PKV_BLOCK_TOKENS;  // 128
 constexpr int kTileTokens = 16;                      // query tokens per CTA
 constexpr int kWarps = kTileTokens / 2;              // 2 tokens x 8 heads = 16 MMA rows a warp
 constexpr int kThreads = kWarps * 32;
@@ -93,13 +99,19 @@ __device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_
 
 __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const PrefillArgs a) {
     __shared__ __align__(128) uint8_t ring[kStages * 2 * kTileBytes];
+    __shared__ int32_t table[kMaxTableBlocks];
 
-    const int tile = gridDim.x - 1 - blockIdx.x;  // longest tiles first
-    const int kv = blockIdx.y;
+    // Longest tiles first over all heads: the hardware starts CTAs in
+    // blockIdx order, so the head varies fastest.
+    const int tile = gridDim.x / kKvHeads - 1 - static_cast<int>(blockIdx.x) / kKvHeads;
+    const int kv = blockIdx.x % kKvHeads;
     const int t0 = tile * kTileTokens;
     const int last_token = min(t0 + kTileTokens - 1, a.tokens - 1);
     const int blocks = (a.start + last_token) / kBlockTokens + 1;  // blocks 0 .. blocks-1
     const int written = a.start + a.tokens;                         // positions below hold K/V
+    // The tile's block ids, staged once (start + tokens <= 2048: at most 128).
+    for (int j = threadIdx.x; j < blocks; j += kThreads) table[j] = a.blocks[j];
+    __syncthreads();
 
     // This thread's copy: 16 bytes (chunk `ch`) of K or V row `key` of each block.
     const int part = threadIdx.x >> 7;  // 0: K, 1: V
@@ -110,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
     const int64_t part_blocks = (static_cast<int64_t>(a.layer) * 2 + part) * a.num_blocks;
     const __half *copy_src = a.pool + kv * kHeadDim + ch * 8;
     auto issue = [&](int j) {
-        const int32_t block = a.blocks[j];
+        const int32_t block = table[j];
         const bool ok = block >= 0 && block < a.num_blocks;
         if (!ok && threadIdx.x == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
         const __half *src =
@@ -167,8 +179,8 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
 
         const uint32_t ktile = ring_base + (j % kStages) * (2 * kTileBytes);
         const uint32_t vtile = ktile + kTileBytes;
-        // kf[ks]: (keys 0-7 | 8-15) x (dims 16ks.. | 16ks+8..); vf[mt]: V^T of dims 16mt..16mt+15.
-        uint32_t kf[4][4], vf[4][4];
+        // kf[ks]: (keys 0-7 | 8-15) x (dims 16ks.. | 16ks+8..).
+        uint32_t kf[4][4];
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
             const int mat = lane >> 3;
@@ -177,6 +189,10 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), kf[ks][0], kf[ks][1], kf[ks][2],
                              kf[ks][3]);
         }
+
+        // vf[mt]: V^T fragments of dims 16mt .. 16mt+15 (loading them after the S MMAs
+        // measured 17% slower: the PV MMAs then wait on them).
+        uint32_t vf[4][4];
 #pragma unroll
         for (int mt = 0; mt < 4; ++mt) {
             const int mat = lane >> 3;
@@ -185,7 +201,6 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             pkv::ldmatrix_x4_trans(vtile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), vf[mt][0], vf[mt][1],
                                    vf[mt][2], vf[mt][3]);
         }
-
         // S = Q . K^T: s[nt] holds keys 8nt + 2t, +1 of rows g (0, 1) and g + 8 (2, 3).
         float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -193,43 +208,54 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             pkv::mma_f16_16816(s[0], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], kf[ks][0], kf[ks][2]);
             pkv::mma_f16_16816(s[1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], kf[ks][1], kf[ks][3]);
         }
-        const int p0 = j * kBlockTokens + 2 * t;
+        if (j * kBlockTokens + kBlockTokens - 1 > lim_a) {  // a diagonal block: mask positions past each row
+            const int p0 = j * kBlockTokens + 2 * t;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+            for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int pos = p0 + 8 * nt + e;
-                s[nt][e] = pos <= lim_a ? s[nt][e] * kScaleLog2 : -INFINITY;
-                s[nt][2 + e] = pos <= lim_b ? s[nt][2 + e] * kScaleLog2 : -INFINITY;
+                for (int e = 0; e < 2; ++e) {
+                    const int pos = p0 + 8 * nt + e;
+                    if (pos > lim_a) s[nt][e] = -INFINITY;
+                    if (pos > lim_b) s[nt][2 + e] = -INFINITY;
+                }
             }
         }
-        // Position 0 is in every row's range and block 0 comes first, so the
-        // running maxima are finite from the first block on.
-        const float mn_a = fmaxf(m_a, quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]))));
-        const float mn_b = fmaxf(m_b, quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]))));
-        const float alpha_a = pkv::exp2_approx(m_a - mn_a);
-        const float alpha_b = pkv::exp2_approx(m_b - mn_b);
-        m_a = mn_a;
-        m_b = mn_b;
+        // Running maxima in log2 units (the scale is positive, so it commutes
+        // with the max).  Position 0 is in every row's range and block 0 comes
+        // first, so they are finite from the first block on.
+        const float mn_a =
+            fmaxf(m_a, quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]))) * kScaleLog2);
+        const float mn_b =
+            fmaxf(m_b, quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]))) * kScaleLog2);
+        if (__any_sync(0xffffffffu, mn_a != m_a || mn_b != m_b)) {  // some row's maximum moved: rescale
+            const float alpha_a = pkv::exp2_approx(m_a - mn_a);
+            const float alpha_b = pkv::exp2_approx(m_b - mn_b);
+            l_a *= alpha_a;
+            l_b *= alpha_b;
+#pragma unroll
+            for (int dt = 0; dt < 8; ++dt) {
+                o[dt][0] *= alpha_a;
+                o[dt][1] *= alpha_a;
+                o[dt][2] *= alpha_b;
+                o[dt][3] *= alpha_b;
+            }
+            m_a = mn_a;
+            m_b = mn_b;
+        }
+        const float shift_a = kWeightShift - m_a;
+        const float shift_b = kWeightShift - m_b;
         __half2 p[2][2];  // p[nt][0]: row g, p[nt][1]: row g + 8 (keys 8nt + 2t, +1)
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-            p[nt][0] = __floats2half2_rn(pkv::exp2_approx(s[nt][0] - mn_a + kWeightShift),
-                                         pkv::exp2_approx(s[nt][1] - mn_a + kWeightShift));
-            p[nt][1] = __floats2half2_rn(pkv::exp2_approx(s[nt][2] - mn_b + kWeightShift),
-                                         pkv::exp2_approx(s[nt][3] - mn_b + kWeightShift));
+            p[nt][0] = __floats2half2_rn(pkv::exp2_approx(fmaf(s[nt][0], kScaleLog2, shift_a)),
+                                         pkv::exp2_approx(fmaf(s[nt][1], kScaleLog2, shift_a)));
+            p[nt][1] = __floats2half2_rn(pkv::exp2_approx(fmaf(s[nt][2], kScaleLog2, shift_b)),
+                                         pkv::exp2_approx(fmaf(s[nt][3], kScaleLog2, shift_b)));
         }
         const float2 fa0 = __half22float2(p[0][0]), fa1 = __half22float2(p[1][0]);
         const float2 fb0 = __half22float2(p[0][1]), fb1 = __half22float2(p[1][1]);
-        l_a = l_a * alpha_a + ((fa0.x + fa0.y) + (fa1.x + fa1.y));
-        l_b = l_b * alpha_b + ((fb0.x + fb0.y) + (fb1.x + fb1.y));
-#pragma unroll
-        for (int dt = 0; dt < 8; ++dt) {
-            o[dt][0] *= alpha_a;
-            o[dt][1] *= alpha_a;
-            o[dt][2] *= alpha_b;
-            o[dt][3] *= alpha_b;
-        }
+        l_a += (fa0.x + fa0.y) + (fa1.x + fa1.y);
+        l_b += (fb0.x + fb0.y) + (fb1.x + fb1.y);
         // O += P . V: P's A fragments are the S accumulators of key tiles 0 and 1.
         const uint32_t a0 = pkv::pack_half2(p[0][0]), a1 = pkv::pack_half2(p[0][1]);
         const uint32_t a2 = pkv::pack_half2(p[1][0]), a3 = pkv::pack_half2(p[1][1]);
@@ -298,7 +324,7 @@ extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32
     args.tokens = tokens;
     args.error_flag = error_flag;
     cudaLaunchConfig_t config = {};
-    config.gridDim = dim3((tokens + kTileTokens - 1) / kTileTokens, kKvHeads);
+    config.gridDim = dim3((tokens + kTileTokens - 1) / kTileTokens * kKvHeads);
     config.blockDim = dim3(kThreads);
     config.dynamicSmemBytes = 0;
     config.stream = static_cast<cudaStream_t>(stream);
