@@ -97,18 +97,41 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(
     }
 }
 
-// gate_up [rows][2 * inter] (gate, then up) -> out [rows][inter].
-__global__ void silu_mul_kernel(const __half *__restrict__ gate_up, __half *__restrict__ out, int64_t rows,
+__device__ __forceinline__ __half silu_times(__half gate, __half up) {
+    const float g = h2f(gate);
+    const __half silu = __float2half_rn(g / (1.0f + expf(-g)));
+    return __float2half_rn(h2f(silu) * h2f(up));
+}
+
+// gate_up [rows][2 * inter] (gate, then up) -> out [rows][inter].  Row
+// blockIdx.y (+ gridDim.y ...), 16-byte chunks of 8 values along x.
+__global__ void silu_mul_kernel(const __half *__restrict__ gate_up, __half *__restrict__ out, int rows,
                                 int inter) {
-    const int64_t total = rows * inter;
-    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += step) {
-        const int64_t row = e / inter;
-        const int col = static_cast<int>(e - row * inter);
-        const float g = h2f(gate_up[row * 2 * inter + col]);
-        const __half silu = __float2half_rn(g / (1.0f + expf(-g)));
-        const __half up = gate_up[row * 2 * inter + inter + col];
-        out[e] = __float2half_rn(h2f(silu) * h2f(up));
+    const int chunks = inter / kChunk;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= chunks) return;
+    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+        const __half *src = gate_up + static_cast<int64_t>(row) * 2 * inter + c * kChunk;
+        const uint4 g = *reinterpret_cast<const uint4 *>(src);
+        const uint4 u = *reinterpret_cast<const uint4 *>(src + inter);
+        const __half *gh = reinterpret_cast<const __half *>(&g);
+        const __half *uh = reinterpret_cast<const __half *>(&u);
+        uint4 r;
+        __half *rh = reinterpret_cast<__half *>(&r);
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) rh[i] = silu_times(gh[i], uh[i]);
+        *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(row) * inter + c * kChunk) = r;
+    }
+}
+
+// Any inter, any alignment: one value a thread.
+__global__ void silu_mul_scalar_kernel(const __half *__restrict__ gate_up, __half *__restrict__ out, int rows,
+                                       int inter) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= inter) return;
+    for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+        const int64_t base = static_cast<int64_t>(row) * 2 * inter;
+        out[static_cast<int64_t>(row) * inter + col] = silu_times(gate_up[base + col], gate_up[base + inter + col]);
     }
 }
 
@@ -143,12 +166,21 @@ extern "C" int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_
         return pkv::fail(PKV_VALUE_ERROR, "silu_mul: bad arguments");
     }
     if (rows == 0) return PKV_OK;
-    const int64_t total = static_cast<int64_t>(rows) * inter;
-    const int threads = 256;
-    const int64_t wanted = (total + threads - 1) / threads;
-    const int grid = static_cast<int>(wanted < 4096 ? wanted : 4096);
-    silu_mul_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half *>(gate_up), static_cast<__half *>(out), rows, inter);
+    const int threads = 128;
+    const auto s = static_cast<cudaStream_t>(stream);
+    const dim3 grid_rows(1, static_cast<unsigned>(rows < 65535 ? rows : 65535));
+    if (inter % kChunk == 0 && aligned16(gate_up) && aligned16(out)) {
+        const int chunks = inter / kChunk;
+        dim3 grid = grid_rows;
+        grid.x = (chunks + threads - 1) / threads;
+        silu_mul_kernel<<<grid, threads, 0, s>>>(static_cast<const __half *>(gate_up), static_cast<__half *>(out),
+                                                 rows, inter);
+    } else {
+        dim3 grid = grid_rows;
+        grid.x = (inter + threads - 1) / threads;
+        silu_mul_scalar_kernel<<<grid, threads, 0, s>>>(static_cast<const __half *>(gate_up),
+                                                        static_cast<__half *>(out), rows, inter);
+    }
     const cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(err));
     return PKV_OK;

@@ -244,7 +244,8 @@ class BatchedDecoder:
         with allocator.prefill_append(request_id, tokens) as chunk:
 
             def attend(index: int, query: Tensor, key: Tensor, value: Tensor) -> Tensor:
-                return chunk.attend(index, chunk.write_layer(index, key, value, query))
+                # Q is rotated in place inside the fused projection's output.
+                return chunk.attend(index, chunk.write_layer(index, key, value, query, in_place=True))
 
             logits = self.forward(input_ids.view(tokens, 1), attend)
         return logits.view(1, tokens, -1)

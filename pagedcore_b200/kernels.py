@@ -91,9 +91,17 @@ def append_kv(
     if query_in is not None:
         if query_out is None or query_in.shape != (layers, tokens, _QUERY_HEADS, _HEAD_DIM):
             raise ValueError("query must be FP16 [layers, tokens, 32, 64] with an output buffer")
-        query_in = query_in.contiguous()
-        if query_out.shape != query_in.shape or not query_out.is_contiguous():
-            raise ValueError("query_out must be a contiguous buffer shaped like query")
+        # In place (query_out is query_in): the kernel reads each 16-byte chunk
+        # once before writing it, through the same strides.
+        in_place = (
+            query_out.data_ptr() == query_in.data_ptr()
+            and query_out.stride() == query_in.stride()
+            and query_out.shape == query_in.shape
+        )
+        if not (in_place and query_in.stride()[2:] == (_HEAD_DIM, 1)):
+            query_in = query_in.contiguous()
+            if query_out.shape != query_in.shape or not query_out.is_contiguous():
+                raise ValueError("query_out must be a contiguous buffer shaped like query, or query itself")
     check(
         lib.pkv_append_kv(
             _ptr(pool),

@@ -187,17 +187,28 @@ class PrefillAppend:
         self._split_batch: DecodeBatch | None = None
 
     @torch.inference_mode()
-    def write_layer(self, layer: int, key: Tensor, value: Tensor, query: Tensor) -> Tensor:
-        """Rotate K and write K/V [T, 4, 64] at `layer`; return Q [T, 32, 64] rotated."""
+    def write_layer(self, layer: int, key: Tensor, value: Tensor, query: Tensor, *, in_place: bool = False) -> Tensor:
+        """Rotate K and write K/V [T, 4, 64] at `layer`; return Q [T, 32, 64] rotated.
+
+        ``in_place=True`` rotates ``query`` itself (its [32, 64] rows must be
+        contiguous; the token stride may be anything, e.g. a view of a fused
+        Q/K/V projection) and returns it.
+        """
         allocator = self._allocator
         allocator._check_worker()
         if type(layer) is not int or not 0 <= layer < _LAYERS:
             raise ValueError("layer_index must identify one of the 22 decoder layers")
-        rotated = torch.empty((1, self.tokens, 32, 64), dtype=torch.float16, device=allocator._pool.device)
+        query_in = query.reshape(1, self.tokens, 32, 64)
+        if in_place:
+            if query.stride()[-2:] != (64, 1) or query_in.data_ptr() != query.data_ptr():
+                raise ValueError("in-place rotation needs query rows of contiguous [32, 64] heads")
+            rotated = query_in
+        else:
+            rotated = torch.empty((1, self.tokens, 32, 64), dtype=torch.float16, device=allocator._pool.device)
         kernels.append_kv(
             allocator._pool, key.reshape(1, self.tokens, 4, 64), value.reshape(1, self.tokens, 4, 64), self.slots,
             layer_begin=layer, error_flag=allocator._error, positions=self.positions, rope_table=allocator._rope,
-            query_in=query.reshape(1, self.tokens, 32, 64), query_out=rotated,
+            query_in=query_in, query_out=rotated,
         )
         return rotated[0]
 

@@ -50,11 +50,12 @@ def test_add_rms_norm_matches_the_eager_residual_add_and_norm(rows) -> None:
     ulp_close(out, rms_norm(before, weight), ulps=2)
 
 
-@pytest.mark.parametrize("inter", [32, 5632])
-def test_silu_mul_matches_the_eager_swiglu_product(inter) -> None:
+@pytest.mark.parametrize("rows, inter", [(64, 32), (64, 5632), (1, 5632), (2047, 5632), (3, 37)])
+def test_silu_mul_matches_the_eager_swiglu_product(rows, inter) -> None:
+    # 16-byte chunks when inter is a multiple of 8, one value a thread otherwise (37).
     device = cuda_device()
-    generator = torch.Generator(device=device).manual_seed(inter)
-    gate_up = 3 * torch.randn(64, 2 * inter, dtype=torch.float16, device=device, generator=generator)
+    generator = torch.Generator(device=device).manual_seed(inter + rows)
+    gate_up = 3 * torch.randn(rows, 2 * inter, dtype=torch.float16, device=device, generator=generator)
     gate, up = gate_up.chunk(2, -1)
     ulp_close(kernels.silu_mul(gate_up), F.silu(gate) * up)
 

@@ -125,3 +125,25 @@ def test_prefill_attention_checks_its_arguments_and_flags_bad_blocks() -> None:
     kernels.prefill_attention(pool, 0, query, bad, 0, out, flag)
     assert int(flag.item()) == 1  # PKV_DEVICE_BAD_BLOCK
     assert torch.isfinite(out).all()
+
+
+def test_in_place_query_rotation_matches_the_copying_one() -> None:
+    # BatchedDecoder.prefill rotates Q inside the fused Q/K/V projection output
+    # (token stride 2560); it must equal the rotation into a fresh buffer.
+    device = cuda_device()
+    allocator = fragmented_allocator(8, 4, device)
+    request = RequestId("q")
+    allocator.create(KVReservation(request, 8))
+    tokens = 100
+    generator = torch.Generator(device=device).manual_seed(9)
+    qkv = torch.randn(tokens, 2560, dtype=torch.float16, device=device, generator=generator)
+    query = qkv[:, :2048].view(tokens, 32, 64)
+    key = qkv[:, 2048:2304].view(tokens, 4, 64)
+    value = qkv[:, 2304:].view(tokens, 4, 64)
+    with allocator.prefill_append(request, tokens) as chunk:
+        copied = chunk.write_layer(2, key, value, query.clone())
+        rotated = chunk.write_layer(2, key, value, query, in_place=True)
+        assert rotated.data_ptr() == qkv.data_ptr() and rotated.stride() == (2560, 64, 1)
+        assert torch.equal(rotated, copied)
+        torch.testing.assert_close(chunk.attend(2, rotated), chunk.attend(2, copied), atol=0.0, rtol=0.0)
+    allocator.check_device_errors()
