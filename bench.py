@@ -40,6 +40,7 @@ LAYERS = 22
 CALIBRATION_STEPS = 8  # staged steps in which KVAllocator(balance="measured") learns its piece weights
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_TENSOR_TFLOPS = 1590.0
+PREFILL_DRAM_BYTES_2047 = 10_504_448  # prefill_attention_kernel, one launch, ncu (read 10.50 MB, write 0)
 
 
 # ---------------------------------------------------------------------------
@@ -1127,7 +1128,11 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
                 "frac": achieved / peak,
                 "flops_per_launch": flops,
                 "launch_us": attention_us,
-                "traffic": None,
+                # DRAM bytes of one launch at 2047 tokens from one ncu capture: the
+                # rotated Q and the layer's K/V read once, the re-reads hit L2.
+                "traffic": PREFILL_DRAM_BYTES_2047 if tokens == 2047 else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 2047 tokens "
+                                  "(profiles/prefill_attention_2047.md)" if tokens == 2047 else None,
             },
             "gpu_launches_attention_per_step": LAYERS,
             "logits_finite": bool(torch.isfinite(logits).all().item()),

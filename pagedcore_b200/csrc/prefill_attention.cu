@@ -9,25 +9,29 @@
 // softmax and sum from FP16 pages, one FP16 rounding of the output):
 //   out[t,h] = sum_{p <= start+t} softmax_p(q[t,h] . K[p, h/8] * 0.125) V[p, h/8]
 //
-// Work split - one CTA per (16-token query tile, KV head): 8 warps, warp w
-// holding tokens 2w and 2w+1 of the tile with the 8 query heads of the KV
-// head as the 16 rows of its MMA tiles (row r: token 2w + r/8, head r%8).
-// The CTA streams the blocks 0 .. (its last position)/16 once, so every K/V
-// block is read once per 128 query rows (the one-token decode kernel reads
-// it once per 8).  Tiles are taken longest first (the last tile of the chunk
-// has the most blocks) across all four heads, so the short ones fill in
-// behind the long ones.
+// Work split - one CTA per (query tile, KV head), 8 warps; a warp holds 2
+// tokens of the tile with the 8 query heads of the KV head as the 16 rows of
+// its MMA tiles (row r: token 2w + r/8, head r%8).  Whole tiles (16 tokens)
+// stream the blocks 0 .. (last position)/16 once, so every K/V block is read
+// once per 128 query rows (the one-token decode kernel reads it once per 8).
+// When whole tiles would not fill one wave (two CTAs per SM), split tiles
+// (8 tokens) halve the key range between two groups of 4 warps, each with its
+// own copy ring and barrier, and merge the two (m, l, O) in shared memory:
+// twice the CTAs, half the longest CTA (measured 17.0 against 24.8 us at 512
+// tokens; at 2047, 102 against 97 us, so whole tiles are kept there).  Tiles
+// are taken longest first across all four heads (the last tile of the chunk
+// has the most blocks), so the short ones fill in behind the long ones.
 //
-// Data movement - the 256 threads each copy one 16-byte chunk of the block's
-// 16 K rows or 16 V rows of this head (cp.async.cg, L2 only: the block is
-// read again by the chunk's other tiles) into shared memory with the 128-byte
-// XOR swizzle (chunk c of row r at c ^ (r & 7)), so the ldmatrix reads are
-// bank-conflict free, through a 4-deep ring of (K, V) tiles (8 deep measured
-// the same); the block ids are staged in shared memory once.  Slots at
-// or past start + tokens (not written yet; they may hold anything) are
-// zero-filled by the copy itself, so 0 * NaN never reaches the PV sum.  No
-// wait in this kernel polls a flag: cp.async.wait_group and __syncthreads
-// complete when the issued copies complete.
+// Data movement - a group's threads each copy one (whole) or two (split)
+// 16-byte chunks of the block's 16 K rows or 16 V rows of this head
+// (cp.async.cg, L2 only: the block is read again by the chunk's other tiles)
+// into shared memory with the 128-byte XOR swizzle (chunk c of row r at
+// c ^ (r & 7)), so the ldmatrix reads are bank-conflict free, through a
+// 4-deep ring of (K, V) tiles (8 deep measured the same); the block ids are
+// staged in shared memory once.  Slots at or past start + tokens (not written
+// yet; they may hold anything) are zero-filled by the copy itself, so 0 * NaN
+// never reaches the PV sum.  No wait in this kernel polls a flag:
+// cp.async.wait_group and the barriers complete when the issued copies do.
 //
 // Math - mma.sync m16n8k16, FP16 in, FP32 accumulate:
 //   S[16 rows x 16 keys]  = Q[16 x 64] . K^T[64 x 16]     (8 MMAs)
@@ -45,6 +49,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "pagedkv.h"
@@ -62,12 +67,23 @@ constexpr int kRowBytes = kHeadDim * 2;              // 128 B: one head of one t
 constexpr int kTileBytes = kBlockTokens * kRowBytes; // 2 KiB: one head of one block
 constexpr int kStages = 4;
 constexpr int kMaxTableBlocks = PKV_CONTEXT_LIMIT / PKV_BLOCK_TOKENS;  // 128
-constexpr int kTileTokens = 16;                      // query tokens per CTA
-constexpr int kWarps = kTileTokens / 2;              // 2 tokens x 8 heads = 16 MMA rows a warp
-constexpr int kThreads = kWarps * 32;
+constexpr int kThreads = 256;
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
 constexpr float kWeightShift = 15.0f;                       // P scaled by 2^15 before FP16
-static_assert(kThreads == 2 * kBlockTokens * (kRowBytes / 16), "one 16-byte copy per thread per block");
+
+// The two CTA shapes.  Whole: a 16-token tile, 8 warps over all of its blocks.
+// Split: an 8-token tile whose key range is halved between two groups of 4
+// warps (each with its own copy ring), merged in shared memory at the end;
+// twice the CTAs for chunks whose whole tiles would not fill the GPU.
+template <bool SPLIT>
+struct Shape {
+    static constexpr int kTileTokens = SPLIT ? 8 : 16;
+    static constexpr int kGroups = SPLIT ? 2 : 1;
+    static constexpr int kGroupWarps = kTileTokens / 2;  // a warp: 2 tokens x 8 heads = 16 MMA rows
+    static constexpr int kGroupThreads = kGroupWarps * 32;
+    static constexpr int kCopies = 2 * kBlockTokens * (kRowBytes / 16) / kGroupThreads;  // 16-byte copies a block
+    static_assert(kGroups * kGroupThreads == kThreads, "every thread belongs to a group");
+};
 static_assert(kGroup == 8, "a KV head's query heads fill 8 MMA rows");
 
 struct PrefillArgs {
@@ -95,44 +111,69 @@ __device__ __forceinline__ float quad_sum(float v) {
     return v + __shfl_xor_sync(0xffffffffu, v, 2);
 }
 
+// Barrier of one split group's 128 threads (ids 1 and 2; __syncthreads is 0).
+__device__ __forceinline__ void group_sync(int group) {
+    if (group) {
+        asm volatile("bar.sync 2, %0;" ::"n"(kThreads / 2) : "memory");
+    } else {
+        asm volatile("bar.sync 1, %0;" ::"n"(kThreads / 2) : "memory");
+    }
+}
+
 __device__ __forceinline__ uint32_t ld32(const __half *p) { return *reinterpret_cast<const uint32_t *>(p); }
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const PrefillArgs a) {
-    __shared__ __align__(128) uint8_t ring[kStages * 2 * kTileBytes];
+    using S = Shape<SPLIT>;
+    __shared__ __align__(128) uint8_t ring[S::kGroups * kStages * 2 * kTileBytes];
     __shared__ int32_t table[kMaxTableBlocks];
 
     // Longest tiles first over all heads: the hardware starts CTAs in
     // blockIdx order, so the head varies fastest.
     const int tile = gridDim.x / kKvHeads - 1 - static_cast<int>(blockIdx.x) / kKvHeads;
     const int kv = blockIdx.x % kKvHeads;
-    const int t0 = tile * kTileTokens;
-    const int last_token = min(t0 + kTileTokens - 1, a.tokens - 1);
+    const int t0 = tile * S::kTileTokens;
+    const int last_token = min(t0 + S::kTileTokens - 1, a.tokens - 1);
     const int blocks = (a.start + last_token) / kBlockTokens + 1;  // blocks 0 .. blocks-1
     const int written = a.start + a.tokens;                         // positions below hold K/V
     // The tile's block ids, staged once (start + tokens <= 2048: at most 128).
     for (int j = threadIdx.x; j < blocks; j += kThreads) table[j] = a.blocks[j];
     __syncthreads();
 
-    // This thread's copy: 16 bytes (chunk `ch`) of K or V row `key` of each block.
-    const int part = threadIdx.x >> 7;  // 0: K, 1: V
-    const int key = (threadIdx.x >> 3) & (kBlockTokens - 1);
-    const int ch = threadIdx.x & 7;
-    const uint32_t ring_base = pkv::smem_addr(ring);
-    const uint32_t copy_dst = ring_base + part * kTileBytes + key * kRowBytes + ((ch ^ (key & 7)) << 4);
+    // This thread's group and its range of blocks (split: group 1 takes the
+    // second half, with the diagonal).
+    const int group = SPLIT ? static_cast<int>(threadIdx.x) / S::kGroupThreads : 0;
+    const int gtid = threadIdx.x % S::kGroupThreads;
+    const int half = (blocks + 1) / 2;
+    const int g_begin = group ? half : 0;
+    const int g_end = SPLIT && !group ? half : blocks;
+    const int g_count = g_end - g_begin;
+    // This thread's copies: kCopies consecutive 16-byte chunks of K or V row `key` of each block.
+    const int first = gtid * S::kCopies;
+    const int part = first >> 7;  // 0: K, 1: V
+    const int key = (first >> 3) & (kBlockTokens - 1);
+    const int ch0 = first & 7;
+    const uint32_t ring_base = pkv::smem_addr(ring) + group * (kStages * 2 * kTileBytes);
+    const uint32_t dst_row = ring_base + part * kTileBytes + key * kRowBytes;
     const int64_t part_blocks = (static_cast<int64_t>(a.layer) * 2 + part) * a.num_blocks;
-    const __half *copy_src = a.pool + kv * kHeadDim + ch * 8;
-    auto issue = [&](int j) {
+    const __half *copy_src = a.pool + kv * kHeadDim + ch0 * 8;
+    auto issue = [&](int jl) {
+        const int j = g_begin + jl;
         const int32_t block = table[j];
         const bool ok = block >= 0 && block < a.num_blocks;
-        if (!ok && threadIdx.x == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
+        if (!ok && gtid == 0) atomicOr(a.error_flag, PKV_DEVICE_BAD_BLOCK);
         const __half *src =
             copy_src + ((part_blocks + (ok ? block : 0)) * kBlockTokens + key) * (kKvHeads * kHeadDim);
         const uint32_t bytes = ok && j * kBlockTokens + key < written ? 16u : 0u;
-        pkv::cp_async_16(copy_dst + (j % kStages) * (2 * kTileBytes), src, bytes);
+        const uint32_t stage = dst_row + (jl % kStages) * (2 * kTileBytes);
+#pragma unroll
+        for (int c = 0; c < S::kCopies; ++c) {
+            pkv::cp_async_16(stage + (((ch0 + c) ^ (key & 7)) << 4), src + 8 * c, bytes);
+        }
     };
 #pragma unroll
-    for (int j = 0; j < kStages - 1; ++j) {
-        if (j < blocks) issue(j);
+    for (int jl = 0; jl < kStages - 1; ++jl) {
+        if (jl < g_count) issue(jl);
         pkv::cp_async_commit();
     }
 
@@ -140,13 +181,13 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
     const int lane = threadIdx.x & 31;
     const int g = lane >> 2;
     const int t = lane & 3;
-    const int token_a = t0 + 2 * warp;  // MMA rows g     (head g of the group)
-    const int token_b = token_a + 1;    // MMA rows g + 8
+    const int token_a = t0 + 2 * (warp % S::kGroupWarps);  // MMA rows g     (head g of the group)
+    const int token_b = token_a + 1;                      // MMA rows g + 8
     const int qa = min(token_a, a.tokens - 1);
     const int qb = min(token_b, a.tokens - 1);
     const int lim_a = a.start + qa;  // last position each row attends to
     const int lim_b = a.start + qb;
-    const int warp_blocks = token_a < a.tokens ? lim_b / kBlockTokens + 1 : 0;
+    const int warp_end = token_a < a.tokens ? min(g_end, lim_b / kBlockTokens + 1) : g_begin;
     const int head = kv * kGroup + g;
 
     // Q as the A operand: (row g | g+8, dims 16ks + 2t, +1 | +8, +9).
@@ -168,16 +209,21 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
 #pragma unroll
     for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
 
-    for (int j = 0; j < blocks; ++j) {
-        // Block j's copies (group j) are complete; every warp is done with the
-        // stage the next copy overwrites (block j - 1's).
+    for (int jl = 0; jl < g_count; ++jl) {
+        const int j = g_begin + jl;
+        // Block j's copies (copy group jl) are complete; every warp of the
+        // group is done with the stage the next copy overwrites.
         pkv::cp_async_wait<kStages - 2>();
-        __syncthreads();
-        if (j + kStages - 1 < blocks) issue(j + kStages - 1);
+        if (SPLIT) {
+            group_sync(group);
+        } else {
+            __syncthreads();
+        }
+        if (jl + kStages - 1 < g_count) issue(jl + kStages - 1);
         pkv::cp_async_commit();
-        if (j >= warp_blocks) continue;
+        if (j >= warp_end) continue;
 
-        const uint32_t ktile = ring_base + (j % kStages) * (2 * kTileBytes);
+        const uint32_t ktile = ring_base + (jl % kStages) * (2 * kTileBytes);
         const uint32_t vtile = ktile + kTileBytes;
         // kf[ks]: (keys 0-7 | 8-15) x (dims 16ks.. | 16ks+8..).
         uint32_t kf[4][4];
@@ -189,7 +235,6 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             pkv::ldmatrix_x4(ktile + tok * kRowBytes + ((chunk ^ (tok & 7)) << 4), kf[ks][0], kf[ks][1], kf[ks][2],
                              kf[ks][3]);
         }
-
         // vf[mt]: V^T fragments of dims 16mt .. 16mt+15 (loading them after the S MMAs
         // measured 17% slower: the PV MMAs then wait on them).
         uint32_t vf[4][4];
@@ -221,15 +266,16 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             }
         }
         // Running maxima in log2 units (the scale is positive, so it commutes
-        // with the max).  Position 0 is in every row's range and block 0 comes
-        // first, so they are finite from the first block on.
+        // with the max).  Whole tiles start at block 0, which holds position 0
+        // of every row, so their maxima are finite from the first block on; in
+        // a split tile's second half a row may have no position yet (-inf).
         const float mn_a =
             fmaxf(m_a, quad_max(fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]))) * kScaleLog2);
         const float mn_b =
             fmaxf(m_b, quad_max(fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]))) * kScaleLog2);
         if (__any_sync(0xffffffffu, mn_a != m_a || mn_b != m_b)) {  // some row's maximum moved: rescale
-            const float alpha_a = pkv::exp2_approx(m_a - mn_a);
-            const float alpha_b = pkv::exp2_approx(m_b - mn_b);
+            const float alpha_a = SPLIT && m_a == mn_a ? 1.f : pkv::exp2_approx(m_a - mn_a);
+            const float alpha_b = SPLIT && m_b == mn_b ? 1.f : pkv::exp2_approx(m_b - mn_b);
             l_a *= alpha_a;
             l_b *= alpha_b;
 #pragma unroll
@@ -242,8 +288,9 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
             m_a = mn_a;
             m_b = mn_b;
         }
-        const float shift_a = kWeightShift - m_a;
-        const float shift_b = kWeightShift - m_b;
+        // With no position yet the row's scores are all -inf: any finite shift gives p = 0.
+        const float shift_a = SPLIT && m_a == -INFINITY ? 0.f : kWeightShift - m_a;
+        const float shift_b = SPLIT && m_b == -INFINITY ? 0.f : kWeightShift - m_b;
         __half2 p[2][2];  // p[nt][0]: row g, p[nt][1]: row g + 8 (keys 8nt + 2t, +1)
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
@@ -266,9 +313,42 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
         }
     }
     pkv::cp_async_wait<0>();
-
     l_a = quad_sum(l_a);
     l_b = quad_sum(l_b);
+
+    if (SPLIT) {
+        // Merge the halves in shared memory (the rings are free once both groups
+        // are past their loops): group 1 leaves (m, l, O), group 0 combines.
+        __syncthreads();
+        float *xo = reinterpret_cast<float *>(ring);          // [group warp][32 values][32 lanes]
+        float *xm = xo + S::kGroupWarps * 32 * 32;             // [group warp][m_a, m_b, l_a, l_b][32 lanes]
+        const int wg = warp % S::kGroupWarps;
+        if (group == 1) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) xo[(wg * 32 + i) * 32 + lane] = o[i / 4][i % 4];
+            xm[(wg * 4 + 0) * 32 + lane] = m_a;
+            xm[(wg * 4 + 1) * 32 + lane] = m_b;
+            xm[(wg * 4 + 2) * 32 + lane] = l_a;
+            xm[(wg * 4 + 3) * 32 + lane] = l_b;
+        }
+        __syncthreads();
+        if (group == 1) return;
+        // Group 0 holds block 0, so its maxima are finite for every stored row.
+        const float m1a = xm[(wg * 4 + 0) * 32 + lane], m1b = xm[(wg * 4 + 1) * 32 + lane];
+        const float big_a = fmaxf(m_a, m1a), big_b = fmaxf(m_b, m1b);
+        const float w0a = pkv::exp2_approx(m_a - big_a), w0b = pkv::exp2_approx(m_b - big_b);
+        const float w1a = m1a == -INFINITY ? 0.f : pkv::exp2_approx(m1a - big_a);
+        const float w1b = m1b == -INFINITY ? 0.f : pkv::exp2_approx(m1b - big_b);
+        l_a = l_a * w0a + xm[(wg * 4 + 2) * 32 + lane] * w1a;
+        l_b = l_b * w0b + xm[(wg * 4 + 3) * 32 + lane] * w1b;
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+            o[dt][0] = o[dt][0] * w0a + xo[(wg * 32 + 4 * dt + 0) * 32 + lane] * w1a;
+            o[dt][1] = o[dt][1] * w0a + xo[(wg * 32 + 4 * dt + 1) * 32 + lane] * w1a;
+            o[dt][2] = o[dt][2] * w0b + xo[(wg * 32 + 4 * dt + 2) * 32 + lane] * w1b;
+            o[dt][3] = o[dt][3] * w0b + xo[(wg * 32 + 4 * dt + 3) * 32 + lane] * w1b;
+        }
+    }
     if (token_a < a.tokens) {
         __half *dst = a.out + token_a * a.out_stride + head * kHeadDim + 2 * t;
 #pragma unroll
@@ -285,6 +365,22 @@ __global__ void __launch_bounds__(kThreads) prefill_attention_kernel(const Prefi
                 __floats2half2_rn(__fdiv_rn(o[dt][2], l_b), __fdiv_rn(o[dt][3], l_b));
         }
     }
+}
+
+// SMs of the current device (cached per device).
+int sm_count() {
+    constexpr int kMaxDevices = 64;
+    static std::atomic<int> cached[kMaxDevices] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return 148;
+    if (device >= 0 && device < kMaxDevices) {
+        const int known = cached[device].load(std::memory_order_relaxed);
+        if (known > 0) return known;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (device >= 0 && device < kMaxDevices && sms > 0) cached[device].store(sms, std::memory_order_relaxed);
+    return sms;
 }
 
 }  // namespace
@@ -324,11 +420,17 @@ extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32
     args.tokens = tokens;
     args.error_flag = error_flag;
     cudaLaunchConfig_t config = {};
-    config.gridDim = dim3((tokens + kTileTokens - 1) / kTileTokens * kKvHeads);
+    // Whole 16-token tiles when they fill at least one wave of two CTAs per
+    // SM, else split tiles (twice the CTAs).
+    const int whole = (tokens + Shape<false>::kTileTokens - 1) / Shape<false>::kTileTokens * kKvHeads;
+    const bool split = whole < 2 * sm_count();
+    const int tile_tokens = split ? Shape<true>::kTileTokens : Shape<false>::kTileTokens;
+    config.gridDim = dim3((tokens + tile_tokens - 1) / tile_tokens * kKvHeads);
     config.blockDim = dim3(kThreads);
     config.dynamicSmemBytes = 0;
     config.stream = static_cast<cudaStream_t>(stream);
-    const cudaError_t e = cudaLaunchKernelEx(&config, prefill_attention_kernel, args);
+    const cudaError_t e = split ? cudaLaunchKernelEx(&config, prefill_attention_kernel<true>, args)
+                                : cudaLaunchKernelEx(&config, prefill_attention_kernel<false>, args);
     if (e != cudaSuccess) {
         return pkv::fail(PKV_CUDA_ERROR, std::string("prefill attention launch failed: ") + cudaGetErrorString(e));
     }
