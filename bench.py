@@ -984,6 +984,43 @@ def run_decoder_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+def _prefill_cpu_baseline(weights, host_ids, sample_tokens: int = 128, budget_s: float = 10.0) -> dict:
+    """The reference's prefill on the host cores: the dense FP16 forward that
+    PagedCore's prefill_paged runs before its append (decoder.py:113-135), as
+    restated by ``pagedcore_b200.decoder.prefill`` (bit-exact with it on CPU),
+    on the first ``sample_tokens`` tokens of the same prompt, repeated for
+    about ``budget_s`` seconds with all of torch's host threads."""
+    import dataclasses
+
+    import torch
+
+    from pagedcore_b200.decoder import prefill as dense_prefill
+
+    def host(layer):
+        return type(layer)(**{f.name: getattr(layer, f.name).cpu() for f in dataclasses.fields(layer)})
+
+    weights_cpu = type(weights)(embedding=weights.embedding.cpu(), layers=tuple(host(x) for x in weights.layers),
+                                final_norm=weights.final_norm.cpu(), lm_head=weights.lm_head.cpu())
+    prompt = host_ids[:, :sample_tokens].clone()
+    with torch.inference_mode():
+        dense_prefill(prompt, weights_cpu)  # warm-up
+        begin, repeats = time.perf_counter(), 0
+        while repeats == 0 or time.perf_counter() - begin < budget_s:
+            dense_prefill(prompt, weights_cpu)
+            repeats += 1
+    seconds = time.perf_counter() - begin
+    tokens = prompt.shape[1]
+    return {
+        "value": repeats * tokens / seconds,
+        "unit": "tokens/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"the first {tokens} tokens of the prompt through the dense FP16 prefill (the reference's "
+                  f"prefill_paged forward), {repeats} times in {seconds:.1f}s; a short prompt spends "
+                  "relatively less on attention than the full one",
+    }
+
+
 def run_prefill_arm(args: argparse.Namespace) -> None:
     """Row f2: a whole prompt prefilled through the pool (``BatchedDecoder.prefill``).
 
@@ -1139,6 +1176,8 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
             "clocks": clocks.summary(),
             "host_affinity": host_affinity,
         }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = _prefill_cpu_baseline(weights, host_ids)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
