@@ -107,9 +107,9 @@ def prefill_paged_fused(
     Unlike ``prefill_paged`` nothing dense is kept: per layer the chunk's K
     (rotated in the write) and V go straight to their pool slots, and the
     causal attention reads them back through the block table with the
-    split-K decode kernel (token t of the chunk is a row of length
-    start + t + 1).  The request may already hold a cache (the chunk continues
-    it).  Attention accumulates in FP32 as paged decode does, so logits match
+    prefill attention kernel (token t of the chunk attends to positions
+    0 .. start + t).  The request may already hold a cache (the chunk
+    continues it).  Attention accumulates in FP32 as paged decode does, so logits match
     the dense FP16 prefill within tolerance, not bit for bit.  Positions are
     published only after the whole forward succeeds.
     """
