@@ -67,3 +67,30 @@ def test_decode_entry_points_reject_a_partition_that_does_not_cover_the_blocks()
         else:
             assert status == _lib.PKV_VALUE_ERROR
             assert b"launch plan does not match" in _lib.lib.pkv_last_error()
+
+
+def test_prefill_attention_rejects_bad_arguments_before_any_launch() -> None:
+    # Every check below returns before a CUDA call, so none needs a GPU.  The
+    # pointers are never dereferenced: each call fails on a size or alignment.
+    lib, value_error = _lib.lib, _lib.PKV_VALUE_ERROR
+    p = 256  # a nonzero, 16-byte aligned stand-in address
+    row = 32 * 64
+
+    def call(layer=0, query=p, query_stride=row, start=0, tokens=1, out=p, out_stride=row, num_blocks=4, pool=p):
+        return lib.pkv_prefill_attention(pool, num_blocks, layer, query, query_stride, p, start, tokens, out,
+                                         out_stride, p, None)
+
+    for kwargs, message in (
+        ({"layer": 22}, b"22 decoder layers"),
+        ({"layer": -1}, b"22 decoder layers"),
+        ({"tokens": 0}, b"positions below 2048"),
+        ({"start": -1}, b"positions below 2048"),
+        ({"start": 2040, "tokens": 9}, b"positions below 2048"),
+        ({"num_blocks": 0}, b"block count"),
+        ({"query": p + 2}, b"misaligned"),
+        ({"query_stride": row - 2}, b"misaligned"),
+        ({"out_stride": row + 1}, b"misaligned"),
+        ({"pool": p + 8}, b"misaligned"),
+    ):
+        assert call(**kwargs) == value_error, kwargs
+        assert message in lib.pkv_last_error(), (kwargs, lib.pkv_last_error())
