@@ -350,7 +350,6 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     from pagedcore_b200 import workloads
-    from pagedcore_b200.attention import paged_decode_attention
     from pagedcore_b200.engine_types import KVReservation, RequestId
     from pagedcore_b200.graph import DecodeStepGraph
     from pagedcore_b200.kv_cache import KVAllocator
