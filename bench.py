@@ -1170,6 +1170,10 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 2047 tokens "
                                   "(profiles/prefill_attention_2047.md)" if tokens == 2047 else None,
             },
+            # This library's kernels per step: per layer two fused norms, the K/V write
+            # (Q rotated in place), the prefill attention and the SwiGLU product; then
+            # the final norm.  The GEMMs and the embedding are library/torch kernels.
+            "gpu_launches": args.steps * (5 * LAYERS + 1),
             "gpu_launches_attention_per_step": LAYERS,
             "logits_finite": bool(torch.isfinite(logits).all().item()),
             "clocks": clocks.summary(),
