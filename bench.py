@@ -27,6 +27,7 @@ import os
 import statistics
 import sys
 import time
+from datetime import timedelta
 from pathlib import Path
 
 import numpy as np
@@ -41,6 +42,10 @@ CALIBRATION_STEPS = 8  # staged steps in which KVAllocator(balance="measured") l
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_TENSOR_TFLOPS = 1590.0
 PREFILL_DRAM_BYTES_2047 = 10_504_448  # prefill_attention_kernel, one launch, ncu (read 10.50 MB, write 0)
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one fused
+# decode-layer launch over its algorithmic bytes, from one capture of the
+# config 4 step; the committed ncu summary of decode_kernel gives the command.
+DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 1.013
 
 
 # ---------------------------------------------------------------------------
@@ -191,17 +196,6 @@ def _peak_tensor() -> tuple[float, str]:
     return FALLBACK_TENSOR_TFLOPS, "fallback"
 
 
-def _traffic_ratio() -> float | None:
-    """ncu DRAM bytes per decode-layer launch / algorithmic bytes, from the committed summary."""
-    path = ROOT / "profiles" / "decode_layer_cfg4.md"
-    if not path.exists():
-        return None
-    for line in path.read_text().splitlines():
-        if line.startswith("traffic_per_algorithmic_byte:"):
-            return float(line.split(":", 1)[1].strip())
-    return None
-
-
 def _bind_host_cores(device: int) -> str:
     """Run this rank on the host cores NVML reports as closest to its GPU.
 
@@ -345,8 +339,6 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     device = torch.device("cuda", local_rank)
     affinity = _bind_host_cores(local_rank)
     if world > 1:
-        from datetime import timedelta
-
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     from pagedcore_b200 import workloads
@@ -354,10 +346,10 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     from pagedcore_b200.graph import DecodeStepGraph
     from pagedcore_b200.kv_cache import KVAllocator
 
-    total_steps = args.warmup + args.steps
     seed = 4 + 1000 * rank
-    # Room for every append of the run: warm-up, plan, timed, e2e warm-up and e2e steps.
-    room = 2 * total_steps + 4 + CALIBRATION_STEPS
+    # Room for every append of the run: calibration, warm-up, plan, the timed
+    # regions, e2e warm-up and e2e steps.
+    room = CALIBRATION_STEPS + args.warmup + 1 + (args.repeats + 1) * args.steps + 2 + 4
     case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=room)
     context_high = 2048 - room
     pool = torch.empty((22, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
@@ -440,18 +432,22 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     # launches delays the next launch by several microseconds, so the layer
     # time below is the timed region's time over its 22 * K layer launches
     # (split + combine + the gaps between them, plus each step's table upload).
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The timed region is repeated `repeats` times, each exactly `steps` steps
+    # bracketed by a barrier and a device synchronisation; `value` is the
+    # median region, the others give the spread.
+    regions = []
     with ClockSampler(local_rank) as clocks:
-        torch.cuda.nvtx.range_push("timed")
-        start.record(stream)
-        for i in range(args.steps):
-            step(*device_inputs[i % 2])
-        end.record(stream)
-        torch.cuda.nvtx.range_pop()
-        barrier()
-    elapsed_ms = start.elapsed_time(end)
-    layer_ms = elapsed_ms
+        for _ in range(args.repeats):
+            barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push("timed")
+            start.record(stream)
+            for i in range(args.steps):
+                step(*device_inputs[i % 2])
+            end.record(stream)
+            torch.cuda.nvtx.range_pop()
+            barrier()
+            regions.append(start.elapsed_time(end))
     allocator.check_device_errors()
 
     # End to end through the public API with host buffers: every step copies
@@ -506,13 +502,21 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     e2e_end.record(stream)
     barrier()
     e2e_ms = e2e_start.elapsed_time(e2e_end)
-    print(f"rank {rank}: timed {elapsed_ms:.2f} ms, e2e {e2e_ms:.2f} ms, host {affinity}", file=sys.stderr, flush=True)
+    print(f"rank {rank}: timed regions {[round(r, 2) for r in regions]} ms, e2e {e2e_ms:.2f} ms, host {affinity}",
+          file=sys.stderr, flush=True)
     allocator.check_device_errors()
 
-    times = torch.tensor([elapsed_ms, e2e_ms, layer_ms], dtype=torch.float64, device=device)
+    times = torch.tensor([*regions, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, layer_ms = times.tolist()
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)  # per region: the slowest rank
+    *regions, e2e_ms = times.tolist()
+    elapsed_ms = statistics.median(regions)
+    layer_ms = elapsed_ms
+
+    # The whole decoder on the same per-GPU batch size, with the token gather
+    # across ranks (its own pool, weights and batch; all ranks take part).
+    del engine
+    decoder = None if args.no_decoder else decoder_leg(args, device, rank, world, local_rank)
 
     if rank == 0:
         tokens = world * SEQUENCES * args.steps
@@ -520,8 +524,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
         peak, peak_kind = _peak_hbm()
         launch_ms = layer_ms / (args.steps * LAYERS)
         achieved = layer_bytes_per_launch / (launch_ms / 1000.0) / 1e9
-        ratio = _traffic_ratio()
-        traffic = None if ratio is None else ratio * layer_bytes_per_launch
+        traffic = DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE * layer_bytes_per_launch
         launches_per_step = LAYERS * (2 if plan_info["grid"] > 1 else 1)  # split + combine
         line = {
             "metric": METRIC,
@@ -555,9 +558,16 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                 "avg_launch_source": "CUDA events around the timed region / (steps x 22 layer launches); "
                                      "includes the combine, the gaps between launches and each step's table upload",
                 "traffic": traffic,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of decode_kernel per launch "
-                                  "over algorithmic bytes (profiles/decode_layer_cfg4.md), times this run's "
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one decode-layer launch "
+                                  "over its algorithmic bytes (1.013, one capture of this step), times this run's "
                                   "algorithmic bytes",
+            },
+            "repeats": {
+                "regions": args.repeats,
+                "ms_per_step": [r / args.steps for r in regions],
+                "median_ms_per_step": elapsed_ms / args.steps,
+                "spread": (max(regions) - min(regions)) / elapsed_ms,
+                "note": "each region exactly `steps` steps between barriers; value is the median region",
             },
             "e2e": {
                 "value": tokens / (e2e_ms / 1000.0),
@@ -572,6 +582,12 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             "clocks": clocks.summary(),
             "host_affinity": affinity,
         }
+        if decoder is not None:
+            line["decoder"] = {
+                "what": "the same per-GPU batch size (256 sequences) through the whole TinyLlama decoder: greedy "
+                        "decode replayed as one CUDA graph per step, token ids all-gathered over NCCL at N > 1",
+                **decoder,
+            }
         if world == 1 and not args.no_cpu_baseline:
             from threadpoolctl import threadpool_limits
 
@@ -606,8 +622,6 @@ def run_stress_arm(args: argparse.Namespace) -> None:
     device = torch.device("cuda", local_rank)
     _bind_host_cores(local_rank)
     if world > 1:
-        from datetime import timedelta
-
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     run = StressRun(device, seed=5 + 1000 * rank)
     if world > 1:
@@ -688,8 +702,6 @@ def run_append_arm(args: argparse.Namespace) -> None:
     device = torch.device("cuda", local_rank)
     host_affinity = _bind_host_cores(local_rank)
     if world > 1:
-        from datetime import timedelta
-
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     seed = 2 + 1000 * rank
     case = workloads.append_case(seed=seed)
@@ -817,8 +829,7 @@ def run_append_arm(args: argparse.Namespace) -> None:
                 "avg_launch_ms": kernel_ms,
                 "traffic": None,
                 "traffic_note": "ncu per launch: reads 1.004 x the K/V input (read once), writes 103-108 of the "
-                                "152 MB written (the rest still dirty in L2 at the launch's end) "
-                                "(profiles/append_kv_cfg2a.md)",
+                                "152 MB written (the rest still dirty in L2 at the launch's end)",
             },
             "e2e": {
                 "value": all_tokens / (e2e_ms / 1000.0),
@@ -862,16 +873,21 @@ def run_append_arm(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
-def run_decoder_arm(args: argparse.Namespace) -> None:
-    """Row f1: the whole TinyLlama decoder step for config 4's batch, replayed as a CUDA graph.
+def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_rank: int) -> dict | None:
+    """Config 4 through the whole TinyLlama decoder: sharded greedy decode with the token gather.
 
-    Random-init TinyLlama weights (the reference publishes no checkpoint here),
-    256 sequences per GPU with contexts U[1, 2048 - room] filled with seeded
-    K/V, one greedy-free step = embedding, 22 x (norm, fused Q/K/V GEMM, fused
-    decode layer, output projection, norm, gate/up GEMM, SwiGLU product, down
-    projection), final norm and LM head (`DecoderStepGraph`).  Reported against
-    HBM: the bytes a step must move (weights read once, the attention's K/V
-    stream and the pool writes) over its time.
+    Random-init TinyLlama weights (the reference publishes no checkpoint
+    here), 256 sequences per GPU (rank r owns batch positions i % N == r of
+    the 256 N-row batch) with contexts U[1, 2048 - room] of seeded K/V.  One
+    step = embedding, 22 x (norm, fused Q/K/V GEMM, fused decode layer,
+    output projection, norm, gate/up GEMM, SwiGLU product, down projection),
+    final norm and LM head, replayed as one CUDA graph (``DecoderStepGraph``),
+    then each row's greedy token (argmax on the device) and, at N > 1, the
+    all-gather of the whole batch's tokens over NCCL (``ShardedGreedyDecoder``,
+    ``StepExchange``): the next step's input ids never leave the device.
+    `e2e`: the same loop as a serving process runs it, the step's ids copied
+    in from pinned host memory and the gathered tokens read back every step.
+    Returns the leg's figures on rank 0 (None elsewhere).
     """
     import torch
     import torch.distributed as dist
@@ -879,51 +895,83 @@ def run_decoder_arm(args: argparse.Namespace) -> None:
     from pagedcore_b200 import workloads
     from pagedcore_b200.decoder import BatchedDecoder
     from pagedcore_b200.engine_types import KVReservation, RequestId
-    from pagedcore_b200.graph import DecoderStepGraph
     from pagedcore_b200.kv_cache import KVAllocator
+    from pagedcore_b200.sharding import ShardedGreedyDecoder, StepExchange, shard
     from pagedcore_b200.weights import random_weights
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    host_affinity = _bind_host_cores(local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     seed = 4 + 1000 * rank
-    room = args.warmup + args.steps + 8
-    lengths = workloads.decode_lengths(seed, SEQUENCES, high=2048 - room).tolist()
+    rows = args.sequences
+    room = CALIBRATION_STEPS + args.warmup + 2 * args.steps + 4
+    lengths = workloads.decode_lengths(seed, rows, high=2048 - room).tolist()
     need = sum(-(-(n + room) // 16) for n in lengths) + 8
     pool = torch.empty((LAYERS, 2, need, 16, 4, 64), dtype=torch.float16, device=device)
     allocator = KVAllocator(pool, validation="incremental", balance="measured")
-    requests = tuple(RequestId(f"s{i}") for i in range(SEQUENCES))
+    batch = tuple(RequestId(f"s{i}") for i in range(rows * world))  # the whole batch, all ranks
+    requests = shard(batch, rank, world)
     generator = torch.Generator(device=device).manual_seed(seed)
     for request, length in zip(requests, lengths, strict=True):
         allocator.create(KVReservation(request, -(-(length + room) // 16)))
         kv = torch.randn(LAYERS, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
         allocator.append(request, kv, kv, rotate=True)
-    weights = random_weights(seed, device)
+    weights = random_weights(seed, device, generator_device=device)
     decoder = BatchedDecoder(weights)
-    graph = DecoderStepGraph(decoder, allocator, rows=SEQUENCES)
-    ids = torch.randint(0, 32000, (SEQUENCES, 1), device=device, generator=generator)
+    exchange = StepExchange(wait=timedelta(seconds=120)) if world > 1 else None
+    sharded = ShardedGreedyDecoder(decoder, allocator, batch, exchange)
+    first = torch.randint(0, 32000, (rows, 1), device=device, generator=generator)
     stream = torch.cuda.current_stream(device)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    ids = first
     for _ in range(CALIBRATION_STEPS + args.warmup):
-        graph.step(ids, requests)
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
+        ids, gathered = sharded.step(ids)
+    barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         start.record(stream)
         for _ in range(args.steps):
-            logits = graph.step(ids, requests)
+            ids, gathered = sharded.step(ids)
         end.record(stream)
-        torch.cuda.synchronize(device)
+        barrier()
     step_ms = start.elapsed_time(end) / args.steps
     allocator.check_device_errors()
+
+    # As a serving loop runs it: this rank's input ids from pinned host memory,
+    # the whole batch's tokens read back (and waited for) every step.
+    host_all = torch.empty(rows * world, dtype=torch.int64).pin_memory()
+    host_in = torch.empty((rows, 1), dtype=torch.int64).pin_memory()
+    host_in.copy_(ids.cpu())
+    staged = torch.empty_like(ids)
+    read = torch.cuda.Event()
+
+    def serve_step() -> None:
+        staged.copy_(host_in, non_blocking=True)
+        _, tokens = sharded.step(staged)
+        host_all.copy_(tokens, non_blocking=True)
+        read.record(stream)
+        read.synchronize()
+        host_in.copy_(host_all[rank::world].view(rows, 1))
+
+    serve_step()
+    serve_step()
+    barrier()
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_start.record(stream)
+    for _ in range(args.steps):
+        serve_step()
+    e2e_end.record(stream)
+    barrier()
+    e2e_ms = e2e_start.elapsed_time(e2e_end) / args.steps
+    allocator.check_device_errors()
+    times = torch.tensor([step_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    step_ms, e2e_ms = (float(x) for x in times.tolist())
+    if rank != 0:
+        return None
     # Bytes a step must move: every weight matrix once (the fused Q/K/V and
     # gate/up copies are what the step reads), the embedding rows, and per
     # layer the attention's K/V stream (the cached tokens, the new one
@@ -933,48 +981,87 @@ def run_decoder_arm(args: argparse.Namespace) -> None:
         (layer.o_proj.numel() + layer.down_proj.numel() + 2 * layer.input_norm.numel()) * 2
         for layer in weights.layers) + weights.lm_head.numel() * 2
     kv_bytes = LAYERS * float((1024 * cached + 4 * ((cached + 15) // 16) + 1024).sum())
-    step_bytes = weight_bytes + kv_bytes + SEQUENCES * 2048 * 2
-    times = torch.tensor([step_ms], dtype=torch.float64, device=device)
+    step_bytes = weight_bytes + kv_bytes + rows * 2048 * 2
+    peak, peak_kind = _peak_hbm()
+    achieved = step_bytes / (step_ms / 1000.0) / 1e9
+    # This library's kernels per step: per layer the two fused residual-add
+    # norms, the decode layer's split and combine launches and the SwiGLU
+    # product, then the final norm.  GEMMs, embedding and argmax are library
+    # kernels; so is the NCCL gather.
+    launches = LAYERS * 5 + 1
+    return {
+        "value": world * rows / (step_ms / 1000.0),
+        "unit": "tokens/s",
+        "ms_per_step": step_ms,
+        "steps": args.steps,
+        "sequences_per_gpu": rows,
+        "contexts": f"U[1, {2048 - room}]",
+        "e2e": {
+            "value": world * rows / (e2e_ms / 1000.0),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": rows * 8,
+            "d2h_bytes_per_step": rows * world * 8,
+            "path": "ShardedGreedyDecoder.step with this rank's ids copied from pinned host memory and the "
+                    "gathered tokens of the whole batch read back and waited for every step",
+        },
+        "token_gather": ("NCCL all_gather_into_tensor of int64 next-token ids every step "
+                         f"({rows * world * 8} B gathered), peers checked in the store every step")
+        if world > 1 else "none at N = 1 (one rank holds the whole batch)",
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "whole decoder step (GEMMs, fused decode layers, norms, argmax, gather)",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "bytes_per_step": step_bytes,
+            "weight_bytes": weight_bytes,
+            "attention_bytes": kv_bytes,
+            "traffic": None,
+        },
+        "gpu_launches": args.steps * launches,
+        "clocks": clocks.summary(),
+    }
+
+
+def run_decoder_arm(args: argparse.Namespace) -> None:
+    """Row f1 / config 4 on the whole model: ``decoder_leg`` as its own line."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    host_affinity = _bind_host_cores(local_rank)
     if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    step_ms = float(times.item())
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    leg = decoder_leg(args, device, rank, world, local_rank)
     if rank == 0:
-        peak, peak_kind = _peak_hbm()
-        achieved = step_bytes / (step_ms / 1000.0) / 1e9
         line = {
-            "metric": "full TinyLlama decoder step tokens/s (row f1: batched decode step)",
-            "value": world * SEQUENCES / (step_ms / 1000.0),
+            "metric": "full TinyLlama decoder greedy decode tokens/s (BASELINE config 4 on the whole model; "
+                      "row f1: batched decode step)",
+            "value": leg["value"],
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": step_ms,
+            "ms_per_step": leg["ms_per_step"],
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (random-init TinyLlama weights N(0, 0.02), seeded K/V caches, random token ids)",
             "config": {
-                "workload": f"{SEQUENCES} sequences per GPU, contexts U[1, {2048 - room}], one token each per step "
-                            "through the whole decoder (22 layers + LM head); each step replayed as one CUDA graph "
-                            "(DecoderStepGraph)",
-                "parallelism": f"dp{world} (independent sequences, weights replicated, no collective)",
+                "workload": f"{args.sequences} sequences per GPU, contexts {leg['contexts']}, one greedy token "
+                            "each per step through the whole decoder (22 layers + LM head) replayed as one CUDA "
+                            "graph, then the batch's tokens gathered over NCCL (N > 1)",
+                "parallelism": f"dp{world} (independent sequences, weights replicated, token ids all-gathered)",
+                "l2": "inputs larger than L2: 2.2 GB of weights and ~5.7 GB of K/V per step",
             },
-            "roofline": {
-                "bound": "hbm",
-                "kernel": "whole decoder step (GEMMs, fused decode layers, norms)",
-                "achieved": achieved,
-                "peak": peak,
-                "peak_kind": peak_kind,
-                "unit": "GB/s",
-                "frac": achieved / peak,
-                "bytes_per_step": step_bytes,
-                "weight_bytes": weight_bytes,
-                "attention_bytes": kv_bytes,
-                "traffic": None,
-            },
-            "logits_finite": bool(torch.isfinite(logits).all().item()),
-            "clocks": clocks.summary(),
+            **{k: leg[k] for k in ("e2e", "roofline", "gpu_launches", "clocks", "token_gather")},
             "host_affinity": host_affinity,
         }
         print(json.dumps(line), flush=True)
@@ -1036,6 +1123,7 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
 
+    from pagedcore_b200 import kernels
     from pagedcore_b200.decoder import BatchedDecoder
     from pagedcore_b200.engine_types import KVReservation, RequestId
     from pagedcore_b200.kv_cache import KVAllocator
@@ -1048,8 +1136,6 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
     device = torch.device("cuda", local_rank)
     host_affinity = _bind_host_cores(local_rank)
     if world > 1:
-        from datetime import timedelta
-
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     seed = 6 + 1000 * rank
     tokens = args.prompt
@@ -1167,13 +1253,15 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
                 # DRAM bytes of one launch at 2047 tokens from one ncu capture: the
                 # rotated Q and the layer's K/V read once, the re-reads hit L2.
                 "traffic": PREFILL_DRAM_BYTES_2047 if tokens == 2047 else None,
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 2047 tokens "
-                                  "(profiles/prefill_attention_2047.md)" if tokens == 2047 else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at 2047 tokens"
+                                  if tokens == 2047 else None,
             },
             # This library's kernels per step: per layer two fused norms, the K/V write
             # (Q rotated in place), the prefill attention and the SwiGLU product; then
-            # the final norm.  The GEMMs and the embedding are library/torch kernels.
-            "gpu_launches": args.steps * (5 * LAYERS + 1),
+            # the final norm.  The GEMMs and the embedding are library/torch kernels,
+            # except that a one-token prompt's projections (Q/K/V, o, gate/up, down per
+            # layer and the LM head) run this library's matrix-vector kernel.
+            "gpu_launches": args.steps * (5 * LAYERS + 1 + (4 * LAYERS + 1 if tokens <= kernels.GEMV_MAX_ROWS else 0)),
             "gpu_launches_attention_per_step": LAYERS,
             "logits_finite": bool(torch.isfinite(logits).all().item()),
             "clocks": clocks.summary(),
@@ -1194,6 +1282,10 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--repeats", type=int, default=3,
+                        help="timed regions of --steps steps each (the line reports the median and the spread)")
+    parser.add_argument("--no-decoder", action="store_true",
+                        help="skip the whole-decoder leg of the default line")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
     parser.add_argument("--workload", choices=("decode", "stress", "append", "decoder", "prefill"), default="decode",

@@ -297,8 +297,10 @@ int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, c
  * plugin host with no workspace callback).  Same arguments and result as
  * pkv_decode_attention minus the workspace: the split partials live in one
  * 8 MiB file-scope device array, which every GPU that loads the library holds
- * until exit.  Limit: the plan's workspace_bytes (pkv_decode_plan) must not
- * exceed 8 MiB (batch + grid up to about 990), else PKV_VALUE_ERROR.  The first
+ * until exit.  Limit: the plan's workspace_bytes (pkv_decode_plan),
+ * 2048 + 16 * grid + 8448 * (batch + grid), must not exceed 8 MiB, i.e.
+ * batch + grid <= (8388608 - 2048 - 16 * grid) / 8448 (991 at the full-wave
+ * grid of 444 on a B200, so batch <= 547), else PKV_VALUE_ERROR.  The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress)
  * and sets the kernel attributes with that device current; make that first
  * call before any stream capture.  All calls share the array and it keeps the
@@ -306,7 +308,9 @@ int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, c
  * call; each call clears the slot-claim counters at its start on `stream`,
  * without allocating), so calls that overlap on the
  * GPU - on different streams, or on one device from different threads - race
- * and must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
+ * and must be serialised by the caller.  The per-slot warp wall-time counters
+ * in the array grow with every call and are never cleared (nothing reads them
+ * on this entry point).  Calls no cudaMalloc / cudaFree. */
 int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                  int64_t query_stride, const int32_t *lengths, const int32_t *prefix,
                                  const int32_t *flat, const int32_t *pieces, const int32_t *row_pieces, int32_t batch,

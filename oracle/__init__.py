@@ -16,4 +16,6 @@ Modules:
 - ``rope``       the FP16 cos/sin table and the FP16 rotation of apply_rope.
 - ``kv_write``   append / write_decode_layer into a numpy FP16 pool.
 - ``attention``  paged_attention's page loop in FP32, and an FP64 dense reference.
+- ``torch_decoder``  the reference's contiguous FP32-attention decoder and its
+  FP32 page loop in torch, to compare the decoder on the same GPU.
 """

@@ -112,8 +112,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, WITH_Q ? 1 : 2) append_kv_k
     const __half *__restrict__ key, const __half *__restrict__ value, int64_t src_layer_stride,
     int64_t src_token_stride, const int32_t *__restrict__ slots,
     const int32_t *__restrict__ positions, int32_t tokens, const __half *__restrict__ rope_cos,
-    const __half *__restrict__ rope_sin, const __half *__restrict__ query_in,
-    __half *__restrict__ query_out, int64_t q_layer_stride, int64_t q_token_stride,
+    const __half *__restrict__ rope_sin,
+    // query_in and query_out may be the same buffer (Q rotated in place):
+    // no __restrict__ on either, each chunk is read before it is written.
+    const __half *query_in, __half *query_out, int64_t q_layer_stride, int64_t q_token_stride,
     int32_t *__restrict__ error_flag) {
     const int lane = threadIdx.x & 31;
     const int head = lane >> 3;

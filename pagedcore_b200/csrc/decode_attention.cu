@@ -72,6 +72,7 @@
 #include "pagedkv.h"
 #include "ptx.cuh"
 #include "status.h"
+#include "tensor_maps.h"
 
 namespace {
 
@@ -86,7 +87,7 @@ constexpr int kTileBytes = kBlockTokens * kRowBytes;     // 2 KiB: one head of o
 constexpr int kStageBytes = 2 * kTileBytes;              // K tile + V tile
 constexpr int kWarps = kKvHeads;
 constexpr int kThreads = kWarps * 32;
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 4;  // mbarriers reserved per warp (the pipeline depth used)
 constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
 constexpr float kWeightShift = 15.0f;                       // P scaled by 2^15 before FP16
@@ -740,7 +741,7 @@ __device__ __forceinline__ void decode_cta(const CUtensorMap &pool_map, const La
 // Three 4-stage CTAs fit an SM's shared memory; the bound holds registers to
 // match (65536 / (3 * 128) = 170 per thread).
 template <int STAGES, bool FUSED>
-__global__ void __launch_bounds__(kThreads, STAGES == 4 ? 3 : 1)
+__global__ void __launch_bounds__(kThreads, 3)
     decode_kernel(const __grid_constant__ CUtensorMap pool_map, const __grid_constant__ LayerArgs a) {
     __shared__ int claimed;
     // The kernel is launched as a programmatic dependent of whatever precedes
@@ -846,77 +847,12 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(
 // Host side: tensor-map cache, launch plan, entry points.
 // ---------------------------------------------------------------------------
 
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+using pkv::EncodeTiled;
+using pkv::encode_fn;
+using pkv::pool_tensor_map;
 
-EncodeTiled encode_fn() {
-    static EncodeTiled fn = [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess) {
-            p = nullptr;
-        }
-        return reinterpret_cast<EncodeTiled>(p);
-    }();
-    return fn;
-}
-
-struct MapKey {
-    uintptr_t pool;
-    int32_t blocks;
-    bool operator==(const MapKey &o) const { return pool == o.pool && blocks == o.blocks; }
-};
-struct MapKeyHash {
-    size_t operator()(const MapKey &k) const { return std::hash<uintptr_t>()(k.pool) ^ (size_t(k.blocks) << 1); }
-};
-
-// 3-D view of the pool for per-head boxes: (dim 64, kv head 4, pool row),
-// strides 128 B (head) and 512 B (row), box 64 x 1 x 16 with the 128-byte
-// swizzle.  Cached per (pool address, block count); the map depends on
-// nothing else.
-int pool_tensor_map(const void *pool, int32_t num_blocks, CUtensorMap *out) {
-    static std::mutex mutex;
-    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-    const MapKey key{reinterpret_cast<uintptr_t>(pool), num_blocks};
-    std::lock_guard<std::mutex> lock(mutex);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-        *out = it->second;
-        return PKV_OK;
-    }
-    EncodeTiled encode = encode_fn();
-    if (encode == nullptr) return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
-    const cuuint64_t rows = static_cast<cuuint64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(kKvHeads), rows};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kRowBytes),
-                                   static_cast<cuuint64_t>(kKvHeads * kRowBytes)};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kHeadDim), 1u, static_cast<cuuint32_t>(kBlockTokens)};
-    const cuuint32_t elem[3] = {1u, 1u, 1u};
-    CUtensorMap map;
-    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(pool), dims,
-                              strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-        return pkv::fail(PKV_CUDA_ERROR, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
-    }
-    cache.emplace(key, map);
-    *out = map;
-    return PKV_OK;
-}
-
-// Pipeline depth per warp (4: three CTAs per SM); PKV_DECODE_STAGES (4, 6 or 8) overrides it.
-int configured_stages() {
-    static int stages = [] {
-        const char *env = std::getenv("PKV_DECODE_STAGES");
-        const int v = env ? std::atoi(env) : 4;
-        return (v == 4 || v == 6 || v == 8) ? v : 4;
-    }();
-    return stages;
-}
+// Pipeline depth per warp: 4 stages keep three CTAs per SM (registers and shared memory).
+constexpr int kStages = 4;
 
 template <int STAGES, bool FUSED>
 int prepare_kernel(int *ctas_per_sm) {
@@ -963,11 +899,7 @@ int device_info(int device, DeviceInfo *info) {
     DeviceInfo d;
     cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device);
     int rc = PKV_OK;
-    switch (configured_stages()) {
-        case 4: rc = prepare_both<4>(&d.ctas_per_sm); break;
-        case 8: rc = prepare_both<8>(&d.ctas_per_sm); break;
-        default: rc = prepare_both<6>(&d.ctas_per_sm); break;
-    }
+    rc = prepare_both<kStages>(&d.ctas_per_sm);
     if (rc == PKV_OK) {
         // The combine needs no shared memory, but an SM that alternates between
         // it and the split kernel would otherwise re-partition L1 and shared
@@ -997,17 +929,8 @@ cudaError_t launch_decode(int grid, const CUtensorMap &map, const LayerArgs &arg
     attribute[0].val.programmaticStreamSerializationAllowed = 1;
     config.attrs = attribute;
     config.numAttrs = 1;
-    switch (configured_stages()) {
-        case 4:
-            config.dynamicSmemBytes = smem_bytes<4>();
-            return cudaLaunchKernelEx(&config, decode_kernel<4, FUSED>, map, args);
-        case 8:
-            config.dynamicSmemBytes = smem_bytes<8>();
-            return cudaLaunchKernelEx(&config, decode_kernel<8, FUSED>, map, args);
-        default:
-            config.dynamicSmemBytes = smem_bytes<6>();
-            return cudaLaunchKernelEx(&config, decode_kernel<6, FUSED>, map, args);
-    }
+    config.dynamicSmemBytes = smem_bytes<kStages>();
+    return cudaLaunchKernelEx(&config, decode_kernel<kStages, FUSED>, map, args);
 }
 
 // The slot claim counters first, then each slot's four warp wall-time
@@ -1255,13 +1178,8 @@ int noalloc_setup(int device, void **scratch) {
             return pkv::fail(PKV_CUDA_ERROR, std::string("no-alloc decode attention: cudaGetSymbolAddress failed: ") +
                                                  cudaGetErrorString(e));
         }
-        const int stages = configured_stages();
-        e = stages == 4 ? cudaFuncSetAttribute(decode_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               smem_bytes<4>())
-            : stages == 8 ? cudaFuncSetAttribute(decode_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 smem_bytes<8>())
-                          : cudaFuncSetAttribute(decode_kernel<6, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 smem_bytes<6>());
+        e = cudaFuncSetAttribute(decode_kernel<kStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem_bytes<kStages>());
         if (e != cudaSuccess) {
             return pkv::fail(PKV_CUDA_ERROR, std::string("no-alloc decode attention: cudaFuncSetAttribute: ") +
                                                  cudaGetErrorString(e));
@@ -1304,8 +1222,8 @@ extern "C" int pkv_decode_attention_noalloc(const void *pool, int32_t num_blocks
         return pkv::fail(PKV_VALUE_ERROR,
                          "no-alloc decode attention: the plan needs " +
                              std::to_string(workspace_bytes_for(batch, grid)) +
-                             " bytes of split partials, over the static scratch limit of 8388608 (8 MiB);"
-                             " use pkv_decode_attention with a workspace");
+                             " bytes of split partials, over the static scratch limit of " +
+                             std::to_string(kNoAllocScratchBytes) + " (8 MiB); use pkv_decode_attention with a workspace");
     }
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);

@@ -436,3 +436,35 @@ extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32
     }
     return PKV_OK;
 }
+
+namespace pkv {
+int launch_prefill_attention_tc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens,
+                                void *out, int64_t out_stride, int32_t *error_flag, cudaStream_t stream);
+}
+
+extern "C" int pkv_prefill_attention_tc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+                                        int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens,
+                                        void *out, int64_t out_stride, int32_t *error_flag, void *stream) {
+    pkv::clear_error();
+    if (pool == nullptr || query == nullptr || blocks == nullptr || out == nullptr || error_flag == nullptr) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: null pointer argument");
+    }
+    if (layer < 0 || layer >= PKV_LAYERS) {
+        return pkv::fail(PKV_VALUE_ERROR, "layer_index must identify one of the 22 decoder layers");
+    }
+    if (num_blocks < 1 || static_cast<int64_t>(PKV_LAYERS) * 2 * num_blocks * kBlockTokens > INT32_MAX) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: pool block count out of range");
+    }
+    if (tokens < 1 || start < 0 || static_cast<int64_t>(start) + tokens > PKV_CONTEXT_LIMIT) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: the chunk must hold 1 or more tokens at positions below 2048");
+    }
+    const int64_t row = static_cast<int64_t>(kQueryHeads) * kHeadDim;
+    if ((reinterpret_cast<uintptr_t>(pool) & 15) || (reinterpret_cast<uintptr_t>(query) & 15) ||
+        (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(blocks) & 3) || query_stride % 8 ||
+        out_stride % 8 || query_stride < row || out_stride < row) {
+        return pkv::fail(PKV_VALUE_ERROR, "prefill attention: misaligned tensor");
+    }
+    return pkv::launch_prefill_attention_tc(pool, num_blocks, layer, query, query_stride, blocks, start, tokens, out,
+                                            out_stride, error_flag, static_cast<cudaStream_t>(stream));
+}

@@ -48,7 +48,11 @@ class StepExchange:
 
     ``store`` is the process group's key-value store (the default group's
     when omitted); ``wait`` bounds how long a rank waits for the others
-    before an exchange.
+    before an exchange.  The ranks announce themselves in the store before
+    every ``check_every``-th exchange (every one by default); a decode loop
+    that must not pay a store round trip per step checks less often, and a
+    failure is then noticed at the next checked step or by the process
+    group's timeout.
     """
 
     def __init__(
@@ -56,7 +60,10 @@ class StepExchange:
         group: dist.ProcessGroup | None = None,
         store: dist.Store | None = None,
         wait: timedelta = timedelta(seconds=60),
+        check_every: int = 1,
     ) -> None:
+        if type(check_every) is not int or check_every < 1:
+            raise ValueError("check_every must be a positive integer")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -64,6 +71,7 @@ class StepExchange:
             store = dist.distributed_c10d._get_default_store()
         self.store = store
         self.wait = wait
+        self.check_every = check_every
         self.step = 0
 
     # -- failure marks ---------------------------------------------------------
@@ -103,7 +111,8 @@ class StepExchange:
         owned = len(shard_positions(count, self.rank, self.world))
         if local.numel() != owned:
             raise ValueError(f"rank {self.rank} owns {owned} of {count} rows, got {local.numel()} ids")
-        self._await_peers()
+        if self.step % self.check_every == 0:
+            self._await_peers()
         per_rank = -(-count // self.world)
         padded = torch.full((per_rank,), -1, dtype=torch.int64, device=local.device)
         padded[:owned] = local
@@ -112,3 +121,44 @@ class StepExchange:
         self.step += 1
         # Rank r's j-th id belongs to batch position r + j*world.
         return gathered.view(self.world, per_rank).t().reshape(-1)[:count]
+
+
+class ShardedGreedyDecoder:
+    """Greedy decode of one batch spread over the ranks, one token per row per step.
+
+    Rank r owns batch positions i % N == r (``shard``): their requests live in
+    this rank's own ``KVAllocator`` (pool, ledger, stream) and its decoder
+    step is a ``graph.DecoderStepGraph`` over them.  Each step picks every
+    owned row's next token on the device (the first maximal logit, the
+    reference's greedy choice, decoder.py:87-100) and the ranks then gather
+    the ids of the whole batch once (``StepExchange.gather_tokens``, NCCL on
+    GPUs): the only data that crosses GPUs.  A rank's own ids feed its next
+    step without leaving the device.
+    """
+
+    def __init__(self, decoder, allocator, requests: Sequence, exchange: StepExchange | None = None, *,
+                 graph=None) -> None:
+        self.exchange = exchange
+        world = 1 if exchange is None else exchange.world
+        rank = 0 if exchange is None else exchange.rank
+        self.count = len(requests)
+        if self.count < world:
+            raise ValueError("every rank needs at least one row of the batch")
+        self.requests = shard(requests, rank, world)
+        if graph is None:  # anything with DecoderStepGraph's step(ids, requests) -> logits [B, 1, V]
+            from pagedcore_b200.graph import DecoderStepGraph
+
+            graph = DecoderStepGraph(decoder, allocator, rows=len(self.requests))
+        self.graph = graph
+
+    @torch.inference_mode()
+    def step(self, input_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """One step for this rank's rows (int64 [owned, 1] ids on its device).
+
+        Returns (this rank's next ids int64 [owned, 1], the whole batch's next
+        ids int64 [count] in batch order); both stay on the device.
+        """
+        logits = self.graph.step(input_ids, self.requests)
+        local = logits[:, 0].argmax(dim=-1)
+        gathered = local if self.exchange is None else self.exchange.gather_tokens(local, self.count)
+        return local.view(-1, 1), gathered

@@ -52,17 +52,20 @@ def random_weights(
     layers: int = LAYERS,
     vocab: int = VOCAB,
     intermediate: int = INTERMEDIATE,
+    generator_device: str | torch.device = "cpu",
 ) -> TinyLlamaWeights:
-    """FP16 weights ~N(0, std) from a CPU generator, norm weights 1.0.
+    """FP16 weights ~N(0, std), norm weights 1.0.
 
-    Every matrix is drawn on the CPU in a fixed order (embedding, then per
-    layer q, k, v, o, gate, up, down, then the LM head), so the same seed
-    gives the same bits on any machine and device.
+    Every matrix is drawn in a fixed order (embedding, then per layer q, k,
+    v, o, gate, up, down, then the LM head).  Drawn on the CPU (the default)
+    the same seed gives the same bits on any machine and device, which the
+    golden fixtures rely on; ``generator_device`` = the GPU draws them there,
+    seconds faster, for throughput runs whose values do not matter.
     """
-    generator = torch.Generator().manual_seed(seed)
+    generator = torch.Generator(device=generator_device).manual_seed(seed)
 
     def matrix(rows: int, cols: int) -> Tensor:
-        values = torch.randn(rows, cols, generator=generator, dtype=torch.float32) * std
+        values = torch.randn(rows, cols, generator=generator, dtype=torch.float32, device=generator_device) * std
         return values.to(torch.float16).to(device)
 
     def norm() -> Tensor:

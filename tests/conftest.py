@@ -60,6 +60,19 @@ def append_small_golden() -> dict[str, np.ndarray]:
 SMALL_CASE = dict(seed=7, num_blocks=48, churn_count=200, prompt_count=3, decode_rows=8, max_prompt=64, churn_tokens=15)
 
 
+def parity_report(test: str, **fields) -> None:
+    """Append one JSON line of a parity test's measured margins to $PKV_PARITY_REPORT, if set.
+
+    The assertions stay in the tests; this only records how close each case
+    came to its bound (worst error over the tolerance, argmax flips, gaps).
+    """
+    path = os.environ.get("PKV_PARITY_REPORT")
+    if not path:
+        return
+    with open(path, "a") as sink:
+        sink.write(json.dumps({"test": test, **fields}) + "\n")
+
+
 def cuda_device():
     import torch
 

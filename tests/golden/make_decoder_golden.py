@@ -33,7 +33,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, os.environ.get("PAGEDCORE_REFERENCE", "/root/reference/src"))
+if not os.environ.get("PAGEDCORE_REFERENCE"):
+    raise SystemExit("set PAGEDCORE_REFERENCE to the reference checkout's src directory (the one holding pagedcore/)")
+sys.path.insert(0, os.environ["PAGEDCORE_REFERENCE"])
 
 from pagedcore.decoder import decode_paged, prefill, prefill_paged  # noqa: E402  (the reference)
 from pagedcore.engine_types import KVReservation, RequestId  # noqa: E402

@@ -36,7 +36,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, os.environ.get("PAGEDCORE_REFERENCE", "/root/reference/src"))
+if not os.environ.get("PAGEDCORE_REFERENCE"):
+    raise SystemExit("set PAGEDCORE_REFERENCE to the reference checkout's src directory (the one holding pagedcore/)")
+sys.path.insert(0, os.environ["PAGEDCORE_REFERENCE"])
 
 from pagedcore.attention import paged_attention  # noqa: E402  (the reference)
 from pagedcore.dense import apply_rope  # noqa: E402

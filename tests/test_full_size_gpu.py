@@ -6,9 +6,9 @@ layer in seconds, so:
 
 - a graph-replayed step (``DecodeStepGraph``: padded tables, per-SM slot
   claims) equals the per-layer ``decode_layer`` launches bit for bit;
-- eight rows (the longest, the shortest and six seeded ones) at two layers
-  match the oracle's FP32 page loop within the reference's tolerance, and
-  their new tokens sit at the oracle's slots with the oracle's RoPE, bit for bit;
+- every row at layers 0 and 21 matches the oracle's FP32 page loop within
+  BASELINE's tolerance, and its new token sits at the oracle's slot with the
+  oracle's RoPE, bit for bit;
 - doubling every cached V and the new tokens' V doubles every output to
   within one FP16 step, and exactly for at least 99.9 % of them.  A power of
   two commutes with this code's FP32 sums and FP16 roundings; the tensor
@@ -29,7 +29,7 @@ from pagedcore_b200 import workloads
 from pagedcore_b200.engine_types import KVReservation, RequestId
 from pagedcore_b200.graph import DecodeStepGraph
 from pagedcore_b200.kv_cache import KVAllocator
-from tests.conftest import cuda_device
+from tests.conftest import cuda_device, parity_report
 
 pytestmark = pytest.mark.gpu
 
@@ -90,31 +90,42 @@ def test_graph_step_equals_per_layer_launches_at_full_size(full_size) -> None:
     assert torch.equal(graphed.pool.view(torch.int16), plain.pool.view(torch.int16))
 
 
-def test_sampled_rows_match_the_oracle_at_full_size(full_size) -> None:
+def test_every_row_matches_the_oracle_at_full_size(full_size) -> None:
+    """All 256 rows at layers 0 and 21 against the oracle's FP32 page loop.
+
+    The bound is BASELINE's max-abs 2e-3 / rel 1e-2 per element; the worst
+    element's error over that bound is reported (PKV_PARITY_REPORT).
+    """
     allocator, requests, positions = full_size["graphed"], full_size["requests"], full_size["positions"]
-    order = np.argsort(positions)
-    rows = sorted({int(order[-1]), int(order[0]), *np.random.default_rng(SEED).choice(ROWS, 6, replace=False).tolist()})
     table = rope.cos_sin_table()
     q = full_size["q"].cpu().numpy()
     k = full_size["k"].cpu().numpy()
     v = full_size["v"].cpu().numpy()
     out = full_size["out_graph"].cpu().numpy()
+    worst = {"ratio": 0.0, "abs": 0.0, "rel": 0.0}
     for layer in (0, 21):
+        layer_pool = allocator.pool[layer].cpu().numpy()[None]  # this layer as a one-layer pool
         q_rot = rope.rotate(q[layer][None], positions, table)[0]
         k_rot = rope.rotate(k[layer][None], positions, table)[0]
-        for row in rows:
-            request = requests[row]
-            blocks = torch.tensor(allocator.block_table(request), dtype=torch.int64, device=allocator.pool.device)
-            # The row's blocks of this layer as a compact one-layer pool.
-            compact = allocator.pool[layer][:, blocks].cpu().numpy()[None]
+        for row, request in enumerate(requests):
+            blocks = allocator.block_table(request)
             length = allocator.cached_length(request)
             assert length == positions[row] + 1
-            expected = oracle_attention.paged_attention(compact, 0, q_rot[row], list(range(len(blocks))), length)
-            np.testing.assert_allclose(out[layer, row].astype(np.float32), expected.astype(np.float32),
-                                       atol=2e-3, rtol=1e-2)
+            expected = oracle_attention.paged_attention(layer_pool, 0, q_rot[row], blocks, length).astype(np.float32)
+            got = out[layer, row].astype(np.float32)
+            error = np.abs(got - expected)
+            worst["ratio"] = max(worst["ratio"], float((error / (2e-3 + 1e-2 * np.abs(expected))).max()))
+            worst["abs"] = max(worst["abs"], float(error.max()))
+            worst["rel"] = max(worst["rel"], float((error / np.maximum(np.abs(expected), 1e-3)).max()))
+            np.testing.assert_allclose(got, expected, atol=2e-3, rtol=1e-2)
             block, slot = divmod(int(positions[row]), 16)
-            assert np.array_equal(compact[0, 0, block, slot].view(np.int16), k_rot[row].view(np.int16))
-            assert np.array_equal(compact[0, 1, block, slot].view(np.int16), v[layer, row].view(np.int16))
+            physical = blocks[block]
+            assert np.array_equal(layer_pool[0, 0, physical, slot].view(np.int16), k_rot[row].view(np.int16))
+            assert np.array_equal(layer_pool[0, 1, physical, slot].view(np.int16), v[layer, row].view(np.int16))
+    parity_report("full_size_every_row", rows=ROWS, layers=[0, 21], worst_tolerance_ratio=worst["ratio"],
+                  worst_abs=worst["abs"], worst_abs_over_2e_3=worst["abs"] / 2e-3,
+                  worst_rel_over_1e_2=worst["rel"] / 1e-2)
+    assert worst["ratio"] <= 1.0
 
 
 def test_doubling_values_doubles_every_output_at_full_size(full_size) -> None:

@@ -53,9 +53,13 @@ def _rank_main(scenario: str, rank: int, port: int, queue) -> None:
 
     store = dist.TCPStore("127.0.0.1", port, WORLD, rank == 0, timeout=timedelta(seconds=30))
     dist.init_process_group("gloo", store=store, rank=rank, world_size=WORLD, timeout=timedelta(seconds=20))
-    exchange = StepExchange(store=store, wait=timedelta(seconds=4 if scenario == "vanish" else 20))
+    exchange = StepExchange(store=store, wait=timedelta(seconds=4 if scenario == "vanish" else 20),
+                            check_every=3 if scenario == "greedy" else 1)
     count = 7
     try:
+        if scenario == "greedy":
+            queue.put((rank, ("ok", _greedy_steps(exchange, count))))
+            return
         # Step 0: every rank contributes ids for its own rows (id = 100 * position).
         mine = torch.from_numpy(shard_positions(count, rank, WORLD) * 100)
         first = exchange.gather_tokens(mine, count).tolist()
@@ -80,6 +84,44 @@ def _rank_main(scenario: str, rank: int, port: int, queue) -> None:
                 queue.put((rank, (type(error).__name__, str(error), time.monotonic() - start)))
     finally:
         dist.destroy_process_group()
+
+
+class _FakeStepGraph:
+    """DecoderStepGraph's step contract on the CPU: logits [B, 1, V] whose
+    greedy choice for request ``rNN`` at input id x is (x + NN) % V (ties to
+    the lower id, as argmax resolves them)."""
+
+    VOCAB = 50
+
+    def __init__(self) -> None:
+        self.calls = []
+
+    def step(self, input_ids, requests):
+        import torch
+
+        self.calls.append(tuple(requests))
+        logits = torch.zeros((len(requests), 1, self.VOCAB), dtype=torch.float16)
+        for row, request in enumerate(requests):
+            best = (int(input_ids[row, 0]) + int(request[1:])) % self.VOCAB
+            logits[row, 0, best:best + 2] = 1.0  # a tie with the next id: the lower one wins
+        return logits
+
+
+def _greedy_steps(exchange, count: int) -> list:
+    import torch
+
+    from pagedcore_b200.sharding import ShardedGreedyDecoder
+
+    requests = tuple(f"r{i}" for i in range(count))
+    graph = _FakeStepGraph()
+    decoder = ShardedGreedyDecoder(None, None, requests, exchange, graph=graph)
+    ids = torch.tensor([[i] for i in range(exchange.rank, count, exchange.world)], dtype=torch.int64)
+    history = []
+    for _ in range(5):
+        ids, gathered = decoder.step(ids)
+        history.append(gathered.tolist())
+    assert all(call == decoder.requests for call in graph.calls)
+    return history
 
 
 def _run(scenario: str) -> dict:
@@ -128,3 +170,18 @@ def test_a_rank_that_leaves_silently_ends_the_wait_with_a_timeout() -> None:
     assert kind == "TimeoutError"
     assert "1 of 2 ranks" in message
     assert 3 < seconds < 20
+
+
+def test_sharded_greedy_decode_gathers_the_whole_batch_every_step() -> None:
+    # Each rank decodes only its own rows; every rank sees all rows' tokens, in
+    # batch order, after every step (peers checked on every third exchange).
+    results = _run("greedy")
+    vocab, count = _FakeStepGraph.VOCAB, 7
+    ids, expected = list(range(count)), []
+    for _ in range(5):
+        ids = [(x + i) % vocab for i, x in enumerate(ids)]
+        expected.append(ids)
+    for rank in range(WORLD):
+        status, history = results[rank]
+        assert status == "ok"
+        assert history == expected

@@ -3,15 +3,20 @@
 Requests reserve their whole context, finish at seeded steps and are replaced;
 admission is credit-bound.  After many iterations the ledger must still audit
 clean, every finished request's blocks must be back, and no kernel may have
-flagged an error.
+flagged an error; decode over blocks that finished requests gave back must
+match the oracle.
 """
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
+import torch
 
+from oracle import attention as oracle_attention
+from oracle import rope
 from pagedcore_b200.stress import StressRun
-from tests.conftest import cuda_device
+from tests.conftest import cuda_device, parity_report
 
 pytestmark = pytest.mark.gpu
 
@@ -29,3 +34,61 @@ def test_churn_keeps_the_ledger_consistent_and_admits_as_credits_free() -> None:
     run.allocator.check_device_errors()
     for request in run.worker.completed:
         assert request.finish_reason is not None
+
+
+def test_decode_after_churn_matches_the_oracle_on_reused_blocks() -> None:
+    """Config 5's point: blocks freed by finished requests are reallocated to
+    new prompts, and decode over them must still read exactly their own data.
+
+    After a churn run, one more graph-replayed decode step for every active
+    request is compared with the oracle's FP32 page loop (layers 0 and 21,
+    BASELINE's 2e-3 / 1e-2), and each new token's K (rotated) and V must sit
+    at the oracle's slot bit for bit.  At least one compared request must own
+    a block that a finished request owned before it.
+    """
+    run = StressRun(cuda_device(), seed=11, rows=16, context=256, new_prompt=64)
+    owners: dict[int, set] = {}  # block -> requests that have held it
+    allocator = run.allocator
+    for _ in range(150):
+        run.iterate()
+        for request in run.worker.active:
+            for block in allocator.block_table(request):
+                owners.setdefault(block, set()).add(request)
+    torch.cuda.synchronize()
+    finished = {request.request_id for request in run.worker.completed + run.worker.finished}
+    for request in run.worker.finished:  # finished in the last iteration: release them now
+        allocator.release_all(request.request_id)
+    run.worker.finished = []
+    active = tuple(run.worker.active)
+    assert len(active) >= 2
+    reused = [r for r in active if any(owners[b] & finished for b in allocator.block_table(r))]
+    assert reused, "no active request holds a block freed by a finished one"
+
+    positions = np.array([allocator.cached_length(r) for r in active], dtype=np.int32)
+    run.graph.step(run.q, run.k, run.k, run.out, active)
+    torch.cuda.synchronize()
+    allocator.check_device_errors()
+    rows = len(active)
+    table = rope.cos_sin_table()
+    q = run.q[:, :rows].cpu().numpy()
+    k = run.k[:, :rows].cpu().numpy()
+    out = run.out[:, :rows].cpu().numpy()
+    worst = 0.0
+    for layer in (0, 21):
+        layer_pool = allocator.pool[layer].cpu().numpy()[None]
+        q_rot = rope.rotate(q[layer][None], positions, table)[0]
+        k_rot = rope.rotate(k[layer][None], positions, table)[0]
+        for row, request in enumerate(active):
+            blocks = allocator.block_table(request)
+            assert allocator.cached_length(request) == positions[row] + 1
+            expected = oracle_attention.paged_attention(layer_pool, 0, q_rot[row], blocks, int(positions[row]) + 1)
+            got = out[layer, row].astype(np.float32)
+            error = np.abs(got - expected.astype(np.float32))
+            worst = max(worst, float((error / (2e-3 + 1e-2 * np.abs(expected.astype(np.float32)))).max()))
+            np.testing.assert_allclose(got, expected.astype(np.float32), atol=2e-3, rtol=1e-2)
+            block, slot = divmod(int(positions[row]), 16)
+            assert np.array_equal(layer_pool[0, 0, blocks[block], slot].view(np.int16), k_rot[row].view(np.int16))
+            assert np.array_equal(layer_pool[0, 1, blocks[block], slot].view(np.int16), k[layer, row].view(np.int16))
+    parity_report("config5_after_churn", rows=rows, rows_on_reused_blocks=len(reused),
+                  completed=len(run.worker.completed), worst_tolerance_ratio=worst)
+    allocator.ledger.audit()

@@ -4,8 +4,9 @@
 device memory (their device memory belongs to another allocator, or their
 plugin interface has no workspace callback): it keeps its split partials in a
 fixed device array instead of a caller workspace.  It must return what
-``pkv_decode_attention`` returns for the same batch, also on a second call
-that finds the previous call's data still in that array.  The file is named to
+``pkv_decode_attention`` returns for the same batch, bit for bit (the same
+kernels, piece tables and merge order), also on a second call that finds the
+previous call's data still in that array, and match the oracle.  The file is named to
 be collected last; it builds its own cache so it also runs alone.
 """
 
@@ -15,6 +16,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import attention as oracle_attention
 from pagedcore_b200 import _lib, kernels, workloads
 from pagedcore_b200.engine_types import KVReservation, RequestId
 from pagedcore_b200.kv_cache import KVAllocator
@@ -82,12 +84,22 @@ def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row() -> None:
         assert _noalloc(allocator, batch, query, layer, actual) == _lib.PKV_OK, _lib.lib.pkv_last_error()
         torch.cuda.synchronize()
         allocator.check_device_errors()
-        torch.testing.assert_close(actual, expected, atol=2e-3, rtol=1e-2)
+        # Same kernels, same piece tables, same merge order: the same bits.
+        assert torch.equal(actual.view(torch.int16), expected.view(torch.int16))
+        # And the reference's algorithm (the oracle's FP32 page loop) on a few rows.
+        layer_pool = allocator.pool[layer].cpu().numpy()[None]
+        got = actual.cpu().numpy().astype(np.float32)
+        q = query.cpu().numpy()
+        for row in (0, int(np.argmax(lengths)), len(lengths) - 1):
+            request = requests[row]
+            reference = oracle_attention.paged_attention(layer_pool, 0, q[row], allocator.block_table(request),
+                                                         allocator.cached_length(request))
+            np.testing.assert_allclose(got[row], reference.astype(np.float32), atol=2e-3, rtol=1e-2)
 
 
 def test_noalloc_entry_rejects_batches_beyond_its_fixed_array() -> None:
-    # Refused on the host before any launch: the plan's partials must fit in 8 MiB
-    # ((batch + grid) * 8448 + grid * 16 bytes).
+    # Refused on the host before any launch: the plan's workspace must fit in 8 MiB
+    # (2048 + 16 * grid + 8448 * (batch + grid) bytes: 990 + 1000 rows is far over).
     cuda_device()
     status = _lib.lib.pkv_decode_attention_noalloc(
         None, 1, 0, None, 0, None, None, None, None, None, 990, 1000, 10, 100, 10, 100, None, 0, None, None
