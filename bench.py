@@ -326,20 +326,18 @@ class ClockSampler:
         return summary
 
 
-def run_gpu_arm(args: argparse.Namespace) -> None:
+def kv_leg(args: argparse.Namespace, device, rank: int, world: int, local_rank: int, sequences: int,
+           repeats: int) -> dict:
+    """Config 4's KV path for `sequences` sequences on this rank (all ranks take part).
+
+    One step = staged append + 22 fused decode-layer launches (Q/K RoPE,
+    new-token KV write, split-K GQA attention + combine) + commit, replayed as
+    CUDA graphs.  Returns the timed regions (max over ranks), the e2e time
+    through the public API with pinned host inputs and outputs, and the
+    algorithmic bytes of one layer launch.
+    """
     import torch
     import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    affinity = _bind_host_cores(local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     from pagedcore_b200 import workloads
     from pagedcore_b200.engine_types import KVReservation, RequestId
@@ -349,8 +347,8 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     seed = 4 + 1000 * rank
     # Room for every append of the run: calibration, warm-up, plan, the timed
     # regions, e2e warm-up and e2e steps.
-    room = CALIBRATION_STEPS + args.warmup + 1 + (args.repeats + 1) * args.steps + 2 + 4
-    case = workloads.decode_case(seed=seed, batch=SEQUENCES, steps=room)
+    room = CALIBRATION_STEPS + args.warmup + 1 + (repeats + 1) * args.steps + 2 + 4
+    case = workloads.decode_case(seed=seed, batch=sequences, steps=room)
     context_high = 2048 - room
     pool = torch.empty((22, 2, case.num_blocks, 16, 4, 64), dtype=torch.float16, device=device)
     allocator = KVAllocator(pool, validation="incremental", balance="measured")
@@ -365,7 +363,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
             allocator.append(rid, zero[:, : op.tokens], zero[:, : op.tokens])
         else:
             allocator.release_all(rid)
-    requests = tuple(RequestId(f"seq{i}") for i in range(SEQUENCES))
+    requests = tuple(RequestId(f"seq{i}") for i in range(sequences))
     for request, length, credits in zip(requests, case.lengths.tolist(), case.credits.tolist()):
         allocator.create(KVReservation(request, credits))
         key = torch.randn(22, length, 4, 64, dtype=torch.float16, device=device, generator=generator)
@@ -375,13 +373,13 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
 
     def inputs(index: int) -> tuple[torch.Tensor, ...]:
         g = torch.Generator(device=device).manual_seed(seed * 7919 + index)
-        q = torch.randn(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device, generator=g)
-        k = torch.randn(22, SEQUENCES, 4, 64, dtype=torch.float16, device=device, generator=g)
-        v = torch.randn(22, SEQUENCES, 4, 64, dtype=torch.float16, device=device, generator=g)
+        q = torch.randn(22, sequences, 32, 64, dtype=torch.float16, device=device, generator=g)
+        k = torch.randn(22, sequences, 4, 64, dtype=torch.float16, device=device, generator=g)
+        v = torch.randn(22, sequences, 4, 64, dtype=torch.float16, device=device, generator=g)
         return q, k, v
 
     device_inputs = [inputs(i) for i in range(2)]
-    out = torch.empty(22, SEQUENCES, 32, 64, dtype=torch.float16, device=device)
+    out = torch.empty(22, sequences, 32, 64, dtype=torch.float16, device=device)
     stream = torch.cuda.current_stream(device)
 
     # Each step's 22 fused decode-layer launches (+ combines) replay as one CUDA
@@ -437,7 +435,7 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     # median region, the others give the spread.
     regions = []
     with ClockSampler(local_rank) as clocks:
-        for _ in range(args.repeats):
+        for _ in range(repeats):
             barrier()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.nvtx.range_push("timed")
@@ -502,20 +500,51 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
     e2e_end.record(stream)
     barrier()
     e2e_ms = e2e_start.elapsed_time(e2e_end)
-    print(f"rank {rank}: timed regions {[round(r, 2) for r in regions]} ms, e2e {e2e_ms:.2f} ms, host {affinity}",
-          file=sys.stderr, flush=True)
+    print(f"rank {rank}: {sequences} sequences, timed regions {[round(r, 2) for r in regions]} ms, "
+          f"e2e {e2e_ms:.2f} ms", file=sys.stderr, flush=True)
     allocator.check_device_errors()
 
     times = torch.tensor([*regions, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)  # per region: the slowest rank
     *regions, e2e_ms = times.tolist()
+    del engine
+    return {"regions": regions, "e2e_ms": e2e_ms, "layer_bytes": layer_bytes_per_launch, "plan": plan_info,
+            "h2d_bytes": h2d_bytes, "d2h_bytes": d2h_bytes, "context_high": context_high, "clocks": clocks.summary(),
+            "case": case, "seed": seed}
+
+
+
+def run_gpu_arm(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    affinity = _bind_host_cores(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    repeats = args.repeats
+    leg = kv_leg(args, device, rank, world, local_rank, SEQUENCES, repeats)
+    regions, e2e_ms, layer_bytes_per_launch, plan_info = leg["regions"], leg["e2e_ms"], leg["layer_bytes"], leg["plan"]
+    h2d_bytes, d2h_bytes, context_high, case, seed = (leg[k] for k in ("h2d_bytes", "d2h_bytes", "context_high",
+                                                                       "case", "seed"))
     elapsed_ms = statistics.median(regions)
     layer_ms = elapsed_ms
+    # BASELINE config 4 spreads 256 sequences over the N GPUs: at N > 1 the
+    # shared-batch point, 256 / N sequences per GPU, is measured too.
+    shared = None
+    if world > 1 and not args.no_shared:
+        shared = kv_leg(args, device, rank, world, local_rank, max(1, 256 // world), 1)
 
     # The whole decoder on the same per-GPU batch size, with the token gather
     # across ranks (its own pool, weights and batch; all ranks take part).
-    del engine
     decoder = None if args.no_decoder else decoder_leg(args, device, rank, world, local_rank)
 
     if rank == 0:
@@ -579,9 +608,21 @@ def run_gpu_arm(args: argparse.Namespace) -> None:
                         "(KVAllocator.append_decode and the 22 decode layers replayed as one CUDA graph)",
             },
             "gpu_launches": args.steps * launches_per_step,
-            "clocks": clocks.summary(),
+            "clocks": leg["clocks"],
             "host_affinity": affinity,
         }
+        if shared is not None:
+            shared_ms = statistics.median(shared["regions"])
+            shared_rows = max(1, 256 // world)
+            shared_launch_ms = shared_ms / (args.steps * LAYERS)
+            line["shared_batch"] = {
+                "what": f"BASELINE config 4's own split: 256 sequences over {world} GPUs, {shared_rows} per GPU",
+                "value": world * shared_rows * args.steps / (shared_ms / 1000.0),
+                "unit": "tokens/s",
+                "ms_per_step": shared_ms / args.steps,
+                "attn_hbm_gbs": shared["layer_bytes"] / (shared_launch_ms / 1000.0) / 1e9,
+                "attn_frac_of_peak": shared["layer_bytes"] / (shared_launch_ms / 1000.0) / 1e9 / peak,
+            }
         if decoder is not None:
             line["decoder"] = {
                 "what": "the same per-GPU batch size (256 sequences) through the whole TinyLlama decoder: greedy "
@@ -1286,6 +1327,8 @@ def main() -> None:
                         help="timed regions of --steps steps each (the line reports the median and the spread)")
     parser.add_argument("--no-decoder", action="store_true",
                         help="skip the whole-decoder leg of the default line")
+    parser.add_argument("--no-shared", action="store_true",
+                        help="skip the shared-batch point (256 / N sequences per GPU) of the default line at N > 1")
     parser.add_argument("--sequences", type=int, default=SEQUENCES,
                         help="sequences per GPU (default: config 4's 256; smaller only for ncu captures)")
     parser.add_argument("--workload", choices=("decode", "stress", "append", "decoder", "prefill"), default="decode",

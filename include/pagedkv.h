@@ -345,6 +345,38 @@ int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter, vo
 int pkv_gemv(const void *x, int64_t x_stride, const void *w, int32_t rows, int32_t n, int32_t k, void *y,
              int64_t y_stride, void *stream);
 
+/* Linear layer of the batched decode step on the tcgen05 tensor cores
+ * (replaces the batch-shaped F.linear of the reference's projections,
+ * dense.py:24-30, 84-109, called row by row in decoder.py:178-198):
+ * y[t][n] = sum_k x[t][k] * w[n][k] for 1..256 rows of x, FP16 operands, FP32
+ * accumulation.  x [rows][k] with rows x_stride elements apart (x_stride a
+ * multiple of 8, x 16-byte aligned), w [n][k] contiguous and 16-byte aligned,
+ * n a multiple of 128 and k of 64.  The K range is cut into `splits` pieces
+ * (1 .. k/64; pkv_linear_splits gives the one that covers the GPU): with one
+ * split y is written as FP16 to out (rows out_stride elements apart); with
+ * more, FP32 partial sums go to partials [splits][rows][n] (16-byte aligned)
+ * and a consumer adds them in split order: pkv_split_sum, or the fused
+ * pkv_add_rms_norm_split / pkv_silu_mul_split.  A timed-out pipeline wait sets
+ * PKV_DEVICE_WAIT_TIMEOUT in error_flag.  Allocates nothing. */
+int pkv_linear_splits(int32_t rows, int32_t n, int32_t k, int32_t *out_splits);
+int pkv_linear(const void *x, int64_t x_stride, const void *w, int32_t rows, int32_t n, int32_t k, int32_t splits,
+               void *out, int64_t out_stride, void *partials, int32_t *error_flag, void *stream);
+
+/* out[t][c] = fp16(sum_s partials[s][t][c]) in split order (the FP16 output
+ * of a split pkv_linear); n a multiple of 4, out rows out_stride apart. */
+int pkv_split_sum(const void *partials, int32_t splits, int32_t rows, int32_t n, void *out, int64_t out_stride,
+                  void *stream);
+
+/* pkv_add_rms_norm with delta = fp16(sum_s partials[s]) of a split pkv_linear
+ * ([splits][rows][dim] FP32): the output projection's or the down
+ * projection's split sums go straight into the next residual add and norm. */
+int pkv_add_rms_norm_split(void *hidden, const void *partials, int32_t splits, const void *weight, void *out,
+                           int32_t rows, int32_t dim, float eps, void *stream);
+
+/* pkv_silu_mul with gate_up = fp16(sum_s partials[s]) of a split gate/up
+ * pkv_linear ([splits][rows][2 * inter] FP32); inter a multiple of 8. */
+int pkv_silu_mul_split(const void *partials, int32_t splits, void *out, int32_t rows, int32_t inter, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "pkv_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
     "pkv_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     "pkv_gemv": (c_int, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]),
+    "pkv_linear_splits": (c_int, [c_int32, c_int32, c_int32, i32p]),
+    "pkv_linear": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+         c_void_p],
+    ),
+    "pkv_split_sum": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p]),
+    "pkv_add_rms_norm_split": (
+        c_int, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p],
+    ),
+    "pkv_silu_mul_split": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p]),
     "pkv_append_kv": (
         c_int,
         [

@@ -31,13 +31,16 @@
 //
 // Math - tensor-core tiles (mma.sync m16n8k16, FP16 in, FP32 accumulate):
 //   S^T[16 tok x 8 heads]  = K[16 x 64] . Q^T[64 x 8]         (4 MMAs)
-//   O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]      (4 MMAs)
+//   O^T[64 dims x 8 heads] += V^T[64 x 16] . P^T[16 x 8]      (2 x 4 MMAs)
 // so the 8-head GQA group fills the N=8 side exactly; the S^T accumulator
 // becomes the P^T operand with two movmatrix transposes.  Softmax is the
-// online (running max) form in base 2 with FP32 state.  P is rounded to FP16
-// for the PV MMA after scaling by 2^15 (p = 2^(s - m + 15) <= 2^15), which
-// keeps weights down to ~2^-24 of the row maximum as normal FP16 numbers; the
-// normaliser l sums the same rounded weights.  Unwritten slots of a row's
+// online (running max) form in base 2 with FP32 state.  The reference keeps
+// P in FP32 (attention.py:46-52); here the FP32 weight p = 2^(s - m + 15)
+// (<= 2^15, so weights down to ~2^-24 of the row maximum stay normal FP16
+// numbers) is split into hi = fp16(p) and lo = fp16(p - hi), and O^T takes
+// both P.V products, which carries P to about 2^-22: FP32 class, where one
+// FP16 operand alone would carry 2^-11.  The normaliser l sums the FP32
+// weights.  Unwritten slots of a row's
 // last block may hold anything (the pool is uninitialised; tests fill it with
 // NaN): their scores are masked to -inf and their V rows are zeroed in shared
 // memory before the PV MMA.
@@ -684,14 +687,20 @@ __device__ __forceinline__ void decode_cta(const CUtensorMap &pool_map, const La
             const float alpha1 = pkv::exp2_approx(m1 - mn1);
             m0 = mn0;
             m1 = mn1;
-            const __half2 p01 = __floats2half2_rn(pkv::exp2_approx(s0 - mn0 + kWeightShift),
-                                                  pkv::exp2_approx(s1 - mn1 + kWeightShift));
-            const __half2 p23 = __floats2half2_rn(pkv::exp2_approx(s2 - mn0 + kWeightShift),
-                                                  pkv::exp2_approx(s3 - mn1 + kWeightShift));
+            const float e0 = pkv::exp2_approx(s0 - mn0 + kWeightShift);
+            const float e1 = pkv::exp2_approx(s1 - mn1 + kWeightShift);
+            const float e2 = pkv::exp2_approx(s2 - mn0 + kWeightShift);
+            const float e3 = pkv::exp2_approx(s3 - mn1 + kWeightShift);
+            // P = hi + lo: the FP16 weight and the FP16 rounding of what it
+            // left out, so the two P.V MMAs carry P to about 2^-22, FP32 class.
+            const __half2 p01 = __floats2half2_rn(e0, e1);
+            const __half2 p23 = __floats2half2_rn(e2, e3);
             const float2 f01 = __half22float2(p01);
             const float2 f23 = __half22float2(p23);
-            l0 = l0 * alpha0 + (f01.x + f23.x);
-            l1 = l1 * alpha1 + (f01.y + f23.y);
+            const __half2 r01 = __floats2half2_rn(e0 - f01.x, e1 - f01.y);
+            const __half2 r23 = __floats2half2_rn(e2 - f23.x, e3 - f23.y);
+            l0 = l0 * alpha0 + (e0 + e2);
+            l1 = l1 * alpha1 + (e1 + e3);
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
                 o[mt][0] *= alpha0;
@@ -702,11 +711,14 @@ __device__ __forceinline__ void decode_cta(const CUtensorMap &pool_map, const La
             // P^T fragments: transpose the (token x head) 8x8 halves.
             const uint32_t b0 = pkv::movmatrix_trans(pkv::pack_half2(p01));
             const uint32_t b1 = pkv::movmatrix_trans(pkv::pack_half2(p23));
+            const uint32_t c0 = pkv::movmatrix_trans(pkv::pack_half2(r01));
+            const uint32_t c1 = pkv::movmatrix_trans(pkv::pack_half2(r23));
 
-            // O^T += V^T . P^T over 16 tokens (4 dim tiles of 16).
+            // O^T += V^T . P^T over 16 tokens (4 dim tiles of 16), hi then lo.
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
                 pkv::mma_f16_16816(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], b0, b1);
+                pkv::mma_f16_16816(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], c0, c1);
             }
         }
         if (failed) break;

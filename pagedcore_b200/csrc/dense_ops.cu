@@ -26,6 +26,8 @@
 #include <string>
 
 #include "pagedkv.h"
+#include "pdl.h"
+#include "ptx.cuh"
 #include "status.h"
 
 namespace {
@@ -39,10 +41,37 @@ __device__ __forceinline__ float h2f(__half x) { return __half2float(x); }
 // kNormThreads * kChunk * kMaxChunksPerThread).
 constexpr int kMaxChunksPerThread = 4;
 
+// fp16 of the sum over `splits` FP32 partial planes (`plane` floats apart) of
+// 8 consecutive values: a split-K linear layer's output, rounded once, as the
+// FP16 GEMM would round it.
+__device__ __forceinline__ uint4 split_sum8(const float *__restrict__ src, int splits, int64_t plane) {
+    float4 a = *reinterpret_cast<const float4 *>(src);
+    float4 b = *reinterpret_cast<const float4 *>(src + 4);
+    for (int s = 1; s < splits; ++s) {
+        const float4 c = *reinterpret_cast<const float4 *>(src + s * plane);
+        const float4 d = *reinterpret_cast<const float4 *>(src + s * plane + 4);
+        a.x += c.x, a.y += c.y, a.z += c.z, a.w += c.w;
+        b.x += d.x, b.y += d.y, b.z += d.z, b.w += d.w;
+    }
+    uint4 r;
+    __half2 *h = reinterpret_cast<__half2 *>(&r);
+    h[0] = __floats2half2_rn(a.x, a.y);
+    h[1] = __floats2half2_rn(a.z, a.w);
+    h[2] = __floats2half2_rn(b.x, b.y);
+    h[3] = __floats2half2_rn(b.z, b.w);
+    return r;
+}
+
+// delta is either FP16 [rows][dim] or, with `partials`, the FP16 sum of
+// `splits` FP32 planes [splits][rows][dim] of a split-K linear layer.
 __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(
-    __half *__restrict__ hidden, const __half *__restrict__ delta, const __half *__restrict__ weight,
-    __half *__restrict__ out, int dim, float eps) {
+    __half *__restrict__ hidden, const __half *__restrict__ delta, const float *__restrict__ partials, int splits,
+    int64_t plane, const __half *__restrict__ weight, __half *__restrict__ out, int dim, float eps) {
     __shared__ float partial[kNormThreads / 32];
+    // Launched as a programmatic dependent (pkv::launch_pdl): let the next
+    // kernel launch, then wait for the previous one before any access.
+    pkv::pdl_launch_dependents();
+    pkv::pdl_wait();
     const int64_t base = static_cast<int64_t>(blockIdx.x) * dim;
     const int chunks = dim / kChunk;
     float v[kMaxChunksPerThread][kChunk];
@@ -53,8 +82,9 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(
         if (c < chunks) {
             uint4 raw = *reinterpret_cast<const uint4 *>(hidden + base + c * kChunk);
             const __half *h = reinterpret_cast<const __half *>(&raw);
-            if (delta != nullptr) {
-                const uint4 draw = *reinterpret_cast<const uint4 *>(delta + base + c * kChunk);
+            if (delta != nullptr || partials != nullptr) {
+                const uint4 draw = partials != nullptr ? split_sum8(partials + base + c * kChunk, splits, plane)
+                                                       : *reinterpret_cast<const uint4 *>(delta + base + c * kChunk);
                 const __half *d = reinterpret_cast<const __half *>(&draw);
                 uint4 sum_raw;
                 __half *s = reinterpret_cast<__half *>(&sum_raw);
@@ -104,16 +134,27 @@ __device__ __forceinline__ __half silu_times(__half gate, __half up) {
 }
 
 // gate_up [rows][2 * inter] (gate, then up) -> out [rows][inter].  Row
-// blockIdx.y (+ gridDim.y ...), 16-byte chunks of 8 values along x.
-__global__ void silu_mul_kernel(const __half *__restrict__ gate_up, __half *__restrict__ out, int rows,
-                                int inter) {
+// blockIdx.y (+ gridDim.y ...), 16-byte chunks of 8 values along x.  With
+// `partials` the gate/up values are the FP16 sums of `splits` FP32 planes
+// [splits][rows][2 * inter] of the split-K gate/up linear layer.
+__global__ void silu_mul_kernel(const __half *__restrict__ gate_up, const float *__restrict__ partials, int splits,
+                                __half *__restrict__ out, int rows, int inter) {
+    pkv::pdl_launch_dependents();
+    pkv::pdl_wait();
     const int chunks = inter / kChunk;
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= chunks) return;
+    const int64_t plane = static_cast<int64_t>(rows) * 2 * inter;
     for (int row = blockIdx.y; row < rows; row += gridDim.y) {
-        const __half *src = gate_up + static_cast<int64_t>(row) * 2 * inter + c * kChunk;
-        const uint4 g = *reinterpret_cast<const uint4 *>(src);
-        const uint4 u = *reinterpret_cast<const uint4 *>(src + inter);
+        const int64_t at = static_cast<int64_t>(row) * 2 * inter + c * kChunk;
+        uint4 g, u;
+        if (partials != nullptr) {
+            g = split_sum8(partials + at, splits, plane);
+            u = split_sum8(partials + at + inter, splits, plane);
+        } else {
+            g = *reinterpret_cast<const uint4 *>(gate_up + at);
+            u = *reinterpret_cast<const uint4 *>(gate_up + at + inter);
+        }
         const __half *gh = reinterpret_cast<const __half *>(&g);
         const __half *uh = reinterpret_cast<const __half *>(&u);
         uint4 r;
@@ -152,10 +193,10 @@ extern "C" int pkv_add_rms_norm(void *hidden, const void *delta, const void *wei
         return pkv::fail(PKV_VALUE_ERROR, "rms norm: tensors must be 16-byte aligned");
     }
     if (rows == 0) return PKV_OK;
-    add_rms_norm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__half *>(hidden), static_cast<const __half *>(delta), static_cast<const __half *>(weight),
-        static_cast<__half *>(out), dim, eps);
-    const cudaError_t err = cudaGetLastError();
+    const cudaError_t err = pkv::launch_pdl(
+        add_rms_norm_kernel, dim3(rows), dim3(kNormThreads), static_cast<cudaStream_t>(stream),
+        static_cast<__half *>(hidden), static_cast<const __half *>(delta), static_cast<const float *>(nullptr), 0,
+        static_cast<int64_t>(0), static_cast<const __half *>(weight), static_cast<__half *>(out), dim, eps);
     if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("rms norm launch failed: ") + cudaGetErrorString(err));
     return PKV_OK;
 }
@@ -173,8 +214,13 @@ extern "C" int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_
         const int chunks = inter / kChunk;
         dim3 grid = grid_rows;
         grid.x = (chunks + threads - 1) / threads;
-        silu_mul_kernel<<<grid, threads, 0, s>>>(static_cast<const __half *>(gate_up), static_cast<__half *>(out),
-                                                 rows, inter);
+        const cudaError_t launched = pkv::launch_pdl(silu_mul_kernel, grid, dim3(threads), s,
+                                                     static_cast<const __half *>(gate_up),
+                                                     static_cast<const float *>(nullptr), 0,
+                                                     static_cast<__half *>(out), rows, inter);
+        if (launched != cudaSuccess) {
+            return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(launched));
+        }
     } else {
         dim3 grid = grid_rows;
         grid.x = (inter + threads - 1) / threads;
@@ -182,6 +228,46 @@ extern "C" int pkv_silu_mul(const void *gate_up, void *out, int32_t rows, int32_
                                                         static_cast<__half *>(out), rows, inter);
     }
     const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(err));
+    return PKV_OK;
+}
+
+extern "C" int pkv_add_rms_norm_split(void *hidden, const void *partials, int32_t splits, const void *weight,
+                                      void *out, int32_t rows, int32_t dim, float eps, void *stream) {
+    pkv::clear_error();
+    if (hidden == nullptr || partials == nullptr || weight == nullptr || out == nullptr || splits < 1) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: hidden, partials, weight and out are required");
+    }
+    if (rows < 0 || dim < kChunk || dim % kChunk || dim > kNormThreads * kChunk * kMaxChunksPerThread) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: dim must be a multiple of 8 up to 8192");
+    }
+    if (!aligned16(hidden) || !aligned16(weight) || !aligned16(out) || !aligned16(partials)) {
+        return pkv::fail(PKV_VALUE_ERROR, "rms norm: tensors must be 16-byte aligned");
+    }
+    if (rows == 0) return PKV_OK;
+    const cudaError_t err = pkv::launch_pdl(
+        add_rms_norm_kernel, dim3(rows), dim3(kNormThreads), static_cast<cudaStream_t>(stream),
+        static_cast<__half *>(hidden), static_cast<const __half *>(nullptr), static_cast<const float *>(partials),
+        splits, static_cast<int64_t>(rows) * dim, static_cast<const __half *>(weight), static_cast<__half *>(out), dim,
+        eps);
+    if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("rms norm launch failed: ") + cudaGetErrorString(err));
+    return PKV_OK;
+}
+
+extern "C" int pkv_silu_mul_split(const void *partials, int32_t splits, void *out, int32_t rows, int32_t inter,
+                                  void *stream) {
+    pkv::clear_error();
+    if (partials == nullptr || out == nullptr || rows < 0 || splits < 1 || inter < kChunk || inter % kChunk ||
+        !aligned16(partials) || !aligned16(out)) {
+        return pkv::fail(PKV_VALUE_ERROR, "silu_mul: bad arguments");
+    }
+    if (rows == 0) return PKV_OK;
+    const int threads = 128;
+    dim3 grid((inter / kChunk + threads - 1) / threads, static_cast<unsigned>(rows < 65535 ? rows : 65535));
+    const cudaError_t err = pkv::launch_pdl(silu_mul_kernel, grid, dim3(threads), static_cast<cudaStream_t>(stream),
+                                            static_cast<const __half *>(nullptr),
+                                            static_cast<const float *>(partials), splits,
+                                            static_cast<__half *>(out), rows, inter);
     if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("silu_mul launch failed: ") + cudaGetErrorString(err));
     return PKV_OK;
 }

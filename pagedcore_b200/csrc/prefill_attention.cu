@@ -385,7 +385,7 @@ int sm_count() {
 
 }  // namespace
 
-extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+extern "C" int pkv_prefill_attention_mma(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                      int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens,
                                      void *out, int64_t out_stride, int32_t *error_flag, void *stream) {
     pkv::clear_error();
@@ -443,7 +443,7 @@ int launch_prefill_attention_tc(const void *pool, int32_t num_blocks, int32_t la
                                 void *out, int64_t out_stride, int32_t *error_flag, cudaStream_t stream);
 }
 
-extern "C" int pkv_prefill_attention_tc(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
+extern "C" int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                                         int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens,
                                         void *out, int64_t out_stride, int32_t *error_flag, void *stream) {
     pkv::clear_error();

@@ -25,13 +25,14 @@
 //   on the next scores while the softmax works on these.
 // - warps 0-3 (128 threads, thread r = row r, TMEM lane r): the softmax.  A
 //   thread reads its row of S_j from TMEM (tcgen05.ld), masks positions past
-//   its token, and keeps the online (running max) state in base 2 in FP32.
-//   When a row's maximum moves, the thread rescales its row of O in TMEM (ld,
-//   multiply, st) once the previous P.V has completed; otherwise O is left
-//   alone.  It writes P_j = 2^(s - m + 15) as FP16 into shared memory in the
-//   MMA's K-major swizzled layout, and the normaliser l sums the same rounded
-//   weights (the decode kernel's scheme: weights down to 2^-24 of the row
-//   maximum stay normal FP16 numbers).  At the end O / l is rounded to FP16.
+//   its token, and keeps the online softmax state in base 2 in FP32: a
+//   reference maximum m that moves only when the row's maximum passes it by
+//   more than 2^8.  It writes P_j = 2^(s - m + 7) (<= 2^15) as FP16 into
+//   shared memory in the MMA's K-major swizzled layout.  The normaliser l is
+//   the MMA's too: P_j times a 64 x 16 matrix of ones accumulates the row sums
+//   of the same FP16 weights in FP32 in TMEM.  When m moves, the thread
+//   rescales its row of O and l in TMEM (ld, multiply, st) once the previous
+//   P.V has completed.  At the end O / l is rounded to FP16.
 //
 // Slots at or past start + tokens hold no K/V yet (the pool may hold
 // anything there): their scores are masked, and their V rows are zeroed in
@@ -72,21 +73,31 @@ constexpr int kQBytes = kRows * kRowBytes;             // 16 KiB
 constexpr int kPBytes = kRows * kStepKeys * 2;         // 16 KiB
 constexpr int kHalfStageBytes = kStepBlocks * kBoxBytes;  // 8 KiB of K (or V)
 constexpr int kStageBytes = 2 * kHalfStageBytes;
-constexpr int kSmemBytes = kQBytes + 2 * kPBytes + kStages * kStageBytes + 1024;  // + alignment slack
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr uint32_t kTmemCols = 256;         // S0 [0, 64), S1 [64, 128), O [128, 192)
+constexpr int kOnesBytes = kBlockTokens * kRowBytes;    // 2 KiB: 16 x 64 FP16 ones (B of the row-sum MMA)
+constexpr int kSmemBytes = kQBytes + 2 * kPBytes + kOnesBytes + kStages * kStageBytes + 1024;  // + alignment slack
+constexpr int kSoftmaxWarps = 4;           // thread r of warps 0-3 owns row r (TMEM lane r)
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kThreads = kSoftmaxThreads + 64;
+constexpr int kProducerWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
+constexpr uint32_t kTmemCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 192), L [192, 208)
 constexpr uint32_t kTmemO = 128;
+constexpr uint32_t kTmemL = 192;     // row sums of P: 16 equal columns
 constexpr uint32_t kWaitPolls = 1u << 24;
 constexpr uint32_t kAbortPolls = 1u << 12;  // once the CTA aborts, later waits give up quickly
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
-constexpr float kWeightShift = 15.0f;
+// P = 2^(s - m + 7) with m the row maximum at its last rescale; m is moved
+// only when a row's maximum exceeds it by more than 2^8, so P <= 2^15 stays
+// inside FP16 while O and l are rescaled at most a few times per row.
+constexpr float kWeightShift = 7.0f;
+constexpr float kRescaleLog2 = 8.0f;
 static_assert(kRows == kTileTokens * (PKV_QUERY_HEADS / kKvHeads), "a tile's rows are its tokens x 8 heads");
 
 // Instruction descriptors: S = Q . K^T (both K-major), O += P . V (P K-major, V MN-major).
 constexpr uint32_t kIdescS = pkv::tc::idesc_f16_f32(kRows, kStepKeys, false, false);
 constexpr uint32_t kIdescO = pkv::tc::idesc_f16_f32(kRows, kHeadDim, false, true);
+// l += P . 1: the row sums of the FP16 weights, accumulated in FP32 by the MMA (N = 16, ones K-major).
+constexpr uint32_t kIdescL = pkv::tc::idesc_f16_f32(kRows, 16, false, false);
 
 struct TcArgs {
     const __half *query;
@@ -147,7 +158,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t *const base_ptr = dyn_smem + (base - raw);
     const uint32_t q_smem = base;
     const uint32_t p_smem = base + kQBytes;                  // P[2]
-    const uint32_t kv_smem = base + kQBytes + 2 * kPBytes;   // stages: K 8 KiB then V 8 KiB
+    const uint32_t ones_smem = base + kQBytes + 2 * kPBytes;  // 16 x 64 FP16 ones
+    const uint32_t kv_smem = ones_smem + kOnesBytes;          // stages: K 8 KiB then V 8 KiB
 
     const int tiles = gridDim.x / kKvHeads;
     const int tile = tiles - 1 - static_cast<int>(blockIdx.x) / kKvHeads;  // longest first
@@ -174,15 +186,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         for (int b = 0; b < 2; ++b) {
             pkv::mbar_init(bar_addr(bars.s_full[b]), 1);
-            pkv::mbar_init(bar_addr(bars.s_empty[b]), 4);
-            pkv::mbar_init(bar_addr(bars.p_full[b]), 4);
+            pkv::mbar_init(bar_addr(bars.s_empty[b]), kSoftmaxWarps);
+            pkv::mbar_init(bar_addr(bars.p_full[b]), kSoftmaxWarps);
             pkv::mbar_init(bar_addr(bars.pv_done[b]), 1);
         }
         pkv::mbar_init(bar_addr(bars.drained), 1);
         abort_flag = 0;
         pkv::fence_barrier_init();
     }
-    if (warp < 4) {
+    if (warp < kSoftmaxWarps) {
         // Q as the A operand: row r = (token r/8, head kv*8 + r%8), 128 B, chunk c at c ^ (r%8).
         const int r = threadIdx.x;
         const int t = min(t0 + (r >> 3), a.tokens - 1);
@@ -193,6 +205,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < 8; ++c) {
             *reinterpret_cast<uint4 *>(row + ((c ^ (r & 7)) << 4)) = src[c];
         }
+        // The ones matrix (16 rows of 64 FP16 1.0, 2 KiB): 16 bytes a thread.
+        reinterpret_cast<uint4 *>(base_ptr + (ones_smem - base))[r] = make_uint4(0x3c003c00u, 0x3c003c00u,
+                                                                                 0x3c003c00u, 0x3c003c00u);
         pkv::fence_proxy_async_smem();  // generic writes -> the MMA's (async proxy) reads
     }
     pkv::tc::fence_before_sync();
@@ -253,9 +268,11 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const uint32_t p_base = p_smem + (i & 1) * kPBytes;
                 const int nb = min(kStepBlocks, nblocks - i * kStepBlocks);
                 for (int kb = 0; kb < nb; ++kb) {
-                    pkv::tc::mma_f16_ss(tmem + kTmemO, pkv::tc::desc_k_major_sw128(p_base + 32 * kb),
-                                        pkv::tc::desc_mn_major_sw128(v_base + kb * kBoxBytes), kIdescO,
-                                        i > 0 || kb > 0);
+                    const uint64_t p_desc = pkv::tc::desc_k_major_sw128(p_base + 32 * kb);
+                    pkv::tc::mma_f16_ss(tmem + kTmemO, p_desc, pkv::tc::desc_mn_major_sw128(v_base + kb * kBoxBytes),
+                                        kIdescO, i > 0 || kb > 0);
+                    pkv::tc::mma_f16_ss(tmem + kTmemL, p_desc, pkv::tc::desc_k_major_sw128(ones_smem + 32 * kb),
+                                        kIdescL, i > 0 || kb > 0);
                 }
                 pkv::tc::commit(bar_addr(bars.pv_done[i & 1]));
                 pkv::tc::commit(bar_addr(bars.kv_empty[st]));
@@ -291,12 +308,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int r = threadIdx.x;
         const int t = t0 + (r >> 3);
         const int pos = a.start + min(t, a.tokens - 1);  // last position this row attends to
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
         const int head = kv * 8 + (r & 7);
         // The step whose last block holds unwritten slots (the chunk's last block), if any.
         const bool ragged = nblocks * kBlockTokens > written;
         const int ragged_step = (nblocks - 1) / kStepBlocks;
-        float m = -INFINITY, l = 0.f;
+        float m = -INFINITY;  // the row maximum at its last rescale (log2 units)
         bool ok = true;
         for (int j = 0; j < steps && ok; ++j) {
             const int b = j & 1;
@@ -306,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             pkv::tc::fence_after_sync();
             uint32_t sr[2][32];
-            pkv::tc::tmem_ld32(tmem + lane_base + b * kStepKeys, sr[0]);
-            pkv::tc::tmem_ld32(tmem + lane_base + b * kStepKeys + 32, sr[1]);
+            pkv::tc::tmem_ld32(lanes + b * kStepKeys, sr[0]);
+            pkv::tc::tmem_ld32(lanes + b * kStepKeys + 32, sr[1]);
             pkv::tc::tmem_wait_ld();
             pkv::tc::fence_before_sync();
             __syncwarp();
@@ -323,51 +340,65 @@ __global__ void __launch_bounds__(kThreads, 2)
                     if (key0 + c > pos) s[c] = -INFINITY;
                 }
             }
-            float mx = s[0];
+            // Row maximum over 8 independent chains: one dependent chain of 64
+            // would cost its full latency every step.
+            float mx8[8];
 #pragma unroll
-            for (int c = 1; c < 64; ++c) mx = fmaxf(mx, s[c]);
-            // Step 0 holds position 0, which every row attends to: m is finite from here on.
-            const float m_new = fmaxf(m, mx * kScaleLog2);
-            if (j >= 1) {
-                // P_{j-1} . V_{j-1} must be complete before O is rescaled and
-                // before P_j overwrites the buffer P_{j-2} used.
+            for (int e = 0; e < 8; ++e) mx8[e] = s[e];
+#pragma unroll
+            for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            // Step 0 holds position 0, which every row attends to: m is finite from step 0 on.
+            const float m_blk = mx * kScaleLog2;
+            const float m_new = m_blk > m + kRescaleLog2 ? m_blk : m;  // m = -inf at step 0: always moves
+            if (j >= 2) {
+                // P_j reuses the buffer of P_{j-2}: that P.V must be complete.
+                if (!warp_wait(bar_addr(bars.pv_done[b]), ((j - 2) >> 1) & 1, &abort_flag, a.error_flag)) {
+                    ok = false;
+                    break;
+                }
+                pkv::tc::fence_after_sync();
+            }
+            // P_j as FP16 (x 2^7) into buffer b, row r, K-major with the 128-byte swizzle.
+            const float shift = kWeightShift - m_new;
+            uint8_t *prow = base_ptr + (p_smem - base) + b * kPBytes + (r >> 3) * 1024 + (r & 7) * kRowBytes;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+                __half2 h[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    h[e] = __floats2half2_rn(pkv::exp2_approx(fmaf(s[8 * c8 + 2 * e], kScaleLog2, shift)),
+                                             pkv::exp2_approx(fmaf(s[8 * c8 + 2 * e + 1], kScaleLog2, shift)));
+                }
+                *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) =
+                    make_uint4(pkv::pack_half2(h[0]), pkv::pack_half2(h[1]), pkv::pack_half2(h[2]),
+                               pkv::pack_half2(h[3]));
+            }
+            if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
+                // Some row's reference maximum moved: rescale its O and l (scaled
+                // by the old one so far) once P_{j-1} . V_{j-1} is in them,
+                // before P_j . V_j adds to them.
                 if (!warp_wait(bar_addr(bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, &abort_flag,
                                a.error_flag)) {
                     ok = false;
                     break;
                 }
                 pkv::tc::fence_after_sync();
-                if (__any_sync(0xffffffffu, m_new != m)) {
-                    const float corr = m_new != m ? pkv::exp2_approx(m - m_new) : 1.f;
+                const float corr = m_new != m ? pkv::exp2_approx(m - m_new) : 1.f;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t o[32];
-                        const uint32_t taddr = tmem + lane_base + kTmemO + 32 * h;
-                        pkv::tc::tmem_ld32(taddr, o);
-                        pkv::tc::tmem_wait_ld();
+                for (int hf = 0; hf < 3; ++hf) {  // O [128, 192) and L [192, 224)
+                    uint32_t o[32];
+                    const uint32_t taddr = lanes + kTmemO + 32 * hf;
+                    pkv::tc::tmem_ld32(taddr, o);
+                    pkv::tc::tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
-                        pkv::tc::tmem_st32(taddr, o);
-                    }
-                    pkv::tc::tmem_wait_st();
-                    l *= corr;
+                    for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
+                    pkv::tc::tmem_st32(taddr, o);
                 }
+                pkv::tc::tmem_wait_st();
             }
             m = m_new;
-            // P_j as FP16 (x 2^15) into buffer b, row r, K-major with the 128-byte swizzle.
-            const float shift = kWeightShift - m;
-            uint8_t *prow = base_ptr + (p_smem - base) + b * kPBytes + (r >> 3) * 1024 + (r & 7) * kRowBytes;
-#pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) {
-                float p[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    p[e] = __half2float(__float2half_rn(pkv::exp2_approx(fmaf(s[8 * c8 + e], kScaleLog2, shift))));
-                    l += p[e];
-                }
-                *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) =
-                    make_uint4(pack2(p[0], p[1]), pack2(p[2], p[3]), pack2(p[4], p[5]), pack2(p[6], p[7]));
-            }
             if (ragged && j == ragged_step) {
                 // Zero the V rows of unwritten slots in the chunk's last block
                 // (thread r: slot r/8, 16-byte chunk r%8) once its copy landed.
@@ -393,9 +424,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             warp_wait(bar_addr(bars.pv_done[(steps - 1) & 1]), ((steps - 1) >> 1) & 1, &abort_flag, a.error_flag)) {
             pkv::tc::fence_after_sync();
             uint32_t o[2][32];
-            pkv::tc::tmem_ld32(tmem + lane_base + kTmemO, o[0]);
-            pkv::tc::tmem_ld32(tmem + lane_base + kTmemO + 32, o[1]);
+            uint32_t sums[16];
+            pkv::tc::tmem_ld32(lanes + kTmemO, o[0]);
+            pkv::tc::tmem_ld32(lanes + kTmemO + 32, o[1]);
+            pkv::tc::tmem_ld16(lanes + kTmemL, sums);
             pkv::tc::tmem_wait_ld();
+            const float l = __uint_as_float(sums[0]);
             if (t < a.tokens) {
                 uint4 *dst = reinterpret_cast<uint4 *>(a.out + t * a.out_stride + head * kHeadDim);
 #pragma unroll

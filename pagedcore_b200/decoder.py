@@ -184,6 +184,8 @@ class BatchedDecoder:
         self.weights = weights
         self.qkv = [torch.cat((layer.q_proj, layer.k_proj, layer.v_proj)) for layer in weights.layers]
         self.gate_up = [torch.cat((layer.gate_proj, layer.up_proj)) for layer in weights.layers]
+        if weights.embedding.is_cuda:
+            kernels.linear_error_flag(weights.embedding.device)  # before any graph capture
 
     def forward(self, input_ids: Tensor, attend: Callable[[int, Tensor, Tensor, Tensor], Tensor]) -> Tensor:
         """The decoder stack for token ids [B, 1]; ``attend(layer, q, k, v)`` is the decode layer.
@@ -196,8 +198,11 @@ class BatchedDecoder:
         the residual add before it in the same kernel (``kernels.add_rms_norm``)
         and SwiGLU's product is one kernel (``kernels.silu_mul``), with the
         rounding points of the reference's eager ops (dense.py:17-21, 84-91).
-        Projections of a single row use this library's matrix-vector kernel
-        (``kernels.linear``), larger batches the library GEMM.
+        Projections run ``kernels.linear``: this library's matrix-vector kernel
+        for a single row, its tcgen05 split-K kernel up to
+        ``kernels.TC_MAX_ROWS`` rows, the library GEMM above.  The output, gate/up and down
+        projections hand their split sums straight to the next fused kernel,
+        which adds them where it would have read the FP16 product.
         """
         weights = self.weights
         batch = input_ids.shape[0]
@@ -205,7 +210,7 @@ class BatchedDecoder:
         hidden = F.embedding(input_ids, weights.embedding).view(batch, HIDDEN)  # updated in place
         x = torch.empty_like(hidden)
         delta = None  # the output still to be added to the residual stream
-        linear = kernels.linear  # the matrix-vector kernel for one row, the library GEMM above
+        linear = kernels.linear
         for index, layer in enumerate(weights.layers):
             kernels.add_rms_norm(hidden, delta, layer.input_norm, x)
             qkv = linear(x, self.qkv[index])
@@ -214,9 +219,10 @@ class BatchedDecoder:
             value = qkv[:, q_width + kv_width :].view(batch, KV_HEADS, HEAD_DIM)
             # RoPE(Q, K) + new-token KV write + attention: one fused launch.
             attention = attend(index, query, key, value)
-            delta = linear(attention.view(batch, HIDDEN), layer.o_proj)
+            delta = linear(attention.view(batch, HIDDEN), layer.o_proj, split_sums=True)
             kernels.add_rms_norm(hidden, delta, layer.post_attention_norm, x)
-            delta = linear(kernels.silu_mul(linear(x, self.gate_up[index])), layer.down_proj)
+            gate_up = linear(x, self.gate_up[index], split_sums=True)
+            delta = linear(kernels.silu_mul(gate_up), layer.down_proj, split_sums=True)
         kernels.add_rms_norm(hidden, delta, weights.final_norm, x)
         return linear(x, weights.lm_head).view(batch, 1, -1)
 

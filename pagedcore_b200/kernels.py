@@ -376,13 +376,53 @@ def decode_layer(
     return out
 
 
-def add_rms_norm(hidden: Tensor, delta: Tensor | None, weight: Tensor, out: Tensor, eps: float = 1e-5) -> Tensor:
+@dataclass(frozen=True, slots=True)
+class SplitSums:
+    """The output of a split-K linear layer before its splits are added:
+    FP32 partial sums [splits, rows, n].  Consumers add the splits in order
+    and round once to FP16, where the FP16 GEMM output would have been."""
+
+    partials: Tensor
+
+    @property
+    def splits(self) -> int:
+        return self.partials.shape[0]
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return self.partials.shape[1], self.partials.shape[2]
+
+    def to_half(self, out: Tensor | None = None) -> Tensor:
+        """fp16(sum of the splits) as [rows, n] (``pkv_split_sum``)."""
+        rows, n = self.shape
+        if out is None:
+            out = torch.empty((rows, n), dtype=torch.float16, device=self.partials.device)
+        check(lib.pkv_split_sum(_ptr(self.partials), self.splits, rows, n, _ptr(out), out.stride(0),
+                                _stream(self.partials.device)))
+        return out
+
+
+def add_rms_norm(hidden: Tensor, delta: Tensor | SplitSums | None, weight: Tensor, out: Tensor,
+                 eps: float = 1e-5) -> Tensor:
     """``hidden += delta`` (FP16, in place, when given), then ``out = rms_norm(hidden) * weight``.
 
     hidden, delta, out FP16 [rows, dim] contiguous; weight FP16 [dim].  Same
-    rounding points as dense.rms_norm after an FP16 residual add.
+    rounding points as dense.rms_norm after an FP16 residual add.  ``delta``
+    may be a linear layer's ``SplitSums``: its splits are added and rounded
+    to FP16 in the same kernel.
     """
     rows, dim = hidden.shape
+    if isinstance(delta, SplitSums):
+        if delta.shape != (rows, dim) or delta.partials.dtype != torch.float32:
+            raise ValueError("delta must hold FP32 split sums [splits, rows, dim]")
+        for name, tensor, shape in (("hidden", hidden, (rows, dim)), ("out", out, (rows, dim)),
+                                    ("weight", weight, (dim,))):
+            if tensor.shape != shape or tensor.dtype != torch.float16 or not tensor.is_contiguous():
+                raise ValueError(f"{name} must be contiguous FP16 {list(shape)}")
+            _require_cuda(name, tensor, hidden.device)
+        check(lib.pkv_add_rms_norm_split(_ptr(hidden), _ptr(delta.partials), delta.splits, _ptr(weight), _ptr(out),
+                                         rows, dim, eps, _stream(hidden.device)))
+        return out
     for name, tensor, shape in (("hidden", hidden, (rows, dim)), ("out", out, (rows, dim)),
                                 ("weight", weight, (dim,)), ("delta", delta, (rows, dim))):
         if tensor is None:
@@ -395,8 +435,18 @@ def add_rms_norm(hidden: Tensor, delta: Tensor | None, weight: Tensor, out: Tens
     return out
 
 
-def silu_mul(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
-    """``silu(gate) * up`` of FP16 gate_up [rows, 2 * inter] (gate first) into [rows, inter]."""
+def silu_mul(gate_up: Tensor | SplitSums, out: Tensor | None = None) -> Tensor:
+    """``silu(gate) * up`` of FP16 gate_up [rows, 2 * inter] (gate first) into [rows, inter].
+
+    ``gate_up`` may be the gate/up layer's ``SplitSums``, added in the same kernel.
+    """
+    if isinstance(gate_up, SplitSums):
+        rows, width = gate_up.shape
+        if out is None:
+            out = torch.empty((rows, width // 2), dtype=torch.float16, device=gate_up.partials.device)
+        check(lib.pkv_silu_mul_split(_ptr(gate_up.partials), gate_up.splits, _ptr(out), rows, width // 2,
+                                     _stream(gate_up.partials.device)))
+        return out
     rows, width = gate_up.shape
     if gate_up.dtype != torch.float16 or not gate_up.is_contiguous() or width % 2:
         raise ValueError("gate_up must be contiguous FP16 [rows, 2 * inter]")
@@ -409,22 +459,82 @@ def silu_mul(gate_up: Tensor, out: Tensor | None = None) -> Tensor:
 # Rows up to which ``linear`` uses the matrix-vector kernel.  Measured on
 # B200 against the library GEMM, weights read from DRAM: at one row it takes
 # 4.6-9.2 us against 7.4-17.3 us on the decoder's Q/K/V, output and down
-# projections, about the same on gate/up and the LM head; from two rows on the
-# library's tensor cores keep its time flat while this kernel turns CUDA-core
-# bound.
+# projections, about the same on gate/up and the LM head; from two rows on it
+# turns CUDA-core bound.
 GEMV_MAX_ROWS = 1
+# Rows up to which ``linear`` uses the tcgen05 split-K kernel.  The kernel
+# takes up to 256 rows (its MMA N limit); measured on B200 over 22 layers of the
+# decoder step's projections, norms and SwiGLU product replayed as one graph,
+# it beats the library GEMM up to 32 rows (37.7 against 40.1 us per layer at
+# 32) and falls behind from 64 rows (51 against 41 at 64, 69 against 47 at 256).
+TC_MAX_ROWS = 32
+
+_linear_errors: dict[int, Tensor] = {}
 
 
-def linear(x: Tensor, weight: Tensor, out: Tensor | None = None) -> Tensor:
+def linear_error_flag(device: torch.device) -> Tensor:
+    """The device error flag of this device's ``pkv_linear`` launches (int32, zero when all is well)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    flag = _linear_errors.get(index)
+    if flag is None:
+        with torch.inference_mode(False):
+            flag = _linear_errors[index] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+    return flag
+
+
+def linear_splits(rows: int, n: int, k: int) -> int:
+    """The K split ``pkv_linear`` uses for this shape on the current device."""
+    splits = ctypes.c_int32()
+    check(lib.pkv_linear_splits(rows, n, k, ctypes.byref(splits)))
+    return splits.value
+
+
+def _tc_shape_ok(x: Tensor, weight: Tensor) -> bool:
+    rows, k = x.shape
+    n = weight.shape[0]
+    return (
+        GEMV_MAX_ROWS < rows <= TC_MAX_ROWS
+        and n % 128 == 0
+        and k % 64 == 0
+        and x.dtype == torch.float16
+        and weight.dtype == torch.float16
+        and weight.shape == (n, k)
+        and weight.is_contiguous()
+        and x.stride(1) == 1
+        and x.stride(0) % 8 == 0
+        and x.data_ptr() % 16 == 0
+        and weight.data_ptr() % 16 == 0
+    )
+
+
+def linear(x: Tensor, weight: Tensor, out: Tensor | None = None, *, split_sums: bool = False) -> Tensor | SplitSums:
     """``F.linear(x, weight)`` for FP16 x [rows, k] and weight [n, k], no bias.
 
-    Up to ``GEMV_MAX_ROWS`` rows run this library's matrix-vector kernel
-    (``pkv_gemv``, bound by reading the weight once); more rows, or shapes it
-    does not take (k not a multiple of 8, unaligned or strided operands), run
-    the library GEMM.  Both sum in FP32 and round once, in different orders.
+    One row runs this library's matrix-vector kernel (``pkv_gemv``, bound by
+    reading the weight once); 2 to ``TC_MAX_ROWS`` rows its tcgen05 kernel
+    (``pkv_linear``, split over K to cover the GPU); other shapes (more rows, k
+    not a multiple of 64, n not of 128, unaligned or strided operands) the
+    library GEMM.  All
+    sum in FP32 and round once, in different orders.  With ``split_sums`` a
+    split tcgen05 layer returns its ``SplitSums`` for a fused consumer
+    (``add_rms_norm``, ``silu_mul``) instead of adding them here.
     """
     rows, k = x.shape
     n = weight.shape[0]
+    if _tc_shape_ok(x, weight):
+        splits = linear_splits(rows, n, k)
+        flag = linear_error_flag(x.device)
+        if splits > 1:
+            partials = torch.empty((splits, rows, n), dtype=torch.float32, device=x.device)
+            check(lib.pkv_linear(_ptr(x), x.stride(0), _ptr(weight), rows, n, k, splits, None, 0, _ptr(partials),
+                                 _ptr(flag), _stream(x.device)))
+            sums = SplitSums(partials)
+            return sums if split_sums and out is None else sums.to_half(out)
+        if out is None:
+            out = torch.empty((rows, n), dtype=torch.float16, device=x.device)
+        check(lib.pkv_linear(_ptr(x), x.stride(0), _ptr(weight), rows, n, k, 1, _ptr(out), out.stride(0), None,
+                             _ptr(flag), _stream(x.device)))
+        return out
     if (
         rows > GEMV_MAX_ROWS
         or k % 8
