@@ -283,10 +283,11 @@ int pkv_decode_layer(void *pool, int32_t num_blocks, int32_t layer, const void *
  * each of the ceil((start+tokens)/16) blocks of the request (its block table);
  * slots at or past start+tokens are never read.  query: rotated FP16
  * [tokens][32][64], rows query_stride elements apart; out likewise with
- * out_stride.  start + tokens <= 2048.  Allocates nothing, no workspace; one
- * launch of ceil(tokens/16) x 4 CTAs, or of ceil(tokens/8) x 4 when that many
- * 16-token tiles would fill less than one wave of the GPU.  Block ids outside
- * [0, num_blocks) set PKV_DEVICE_BAD_BLOCK and read as zeros. */
+ * out_stride; pool, query and out 16-byte aligned, both strides multiples of
+ * 8.  start + tokens <= 2048.  Allocates nothing, no workspace; one launch of
+ * min(ceil(tokens/16) x 4, 2 x SMs) persistent CTAs on the tensor cores
+ * (tcgen05).  Block ids outside [0, num_blocks) set PKV_DEVICE_BAD_BLOCK and
+ * read as zeros. */
 int pkv_prefill_attention(const void *pool, int32_t num_blocks, int32_t layer, const void *query,
                           int64_t query_stride, const int32_t *blocks, int32_t start, int32_t tokens, void *out,
                           int64_t out_stride, int32_t *error_flag, void *stream);

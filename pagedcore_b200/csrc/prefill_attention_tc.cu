@@ -90,9 +90,8 @@ constexpr int kBlockElems = kBlockTokens * kKvHeads * kHeadDim;  // one block of
 constexpr int kKCopyLag = 2;
 constexpr int kVCopyLag = 1;
 constexpr int kQBytes = kRows * kRowBytes;             // 16 KiB
-constexpr int kPBytes = kRows * kStepKeys * 2;         // 16 KiB
 constexpr int kRingBytes = kStepBlocks * kBoxBytes;    // 8 KiB: one step's K (or V)
-constexpr int kSmemBytes = kQBytes + 2 * kPBytes + (kKStages + kVStages) * kRingBytes + 1024;  // + alignment slack
+constexpr int kSmemBytes = kQBytes + (kKStages + kVStages) * kRingBytes + 1024;  // + alignment slack
 constexpr int kSoftmaxWarps = 4;           // thread r of warps 0-3 owns row r (TMEM lane r)
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kThreads = kSoftmaxThreads + 128;
@@ -100,9 +99,15 @@ constexpr int kKProducerWarp = kSoftmaxWarps;
 constexpr int kMmaWarp = kSoftmaxWarps + 1;  // issues S; owns the TMEM allocation
 constexpr int kVProducerWarp = kSoftmaxWarps + 2;
 constexpr int kPvWarp = kSoftmaxWarps + 3;   // issues P.V
-constexpr uint32_t kTmemCols = 256;  // S0 [0, 64), S1 [64, 128), O [128, 192)
-constexpr uint32_t kTmemO = 128;
+// TMEM columns: S buffers b = 0, 1, 2 at [64 b, 64 b + 64) (FP32 S_g in buffer
+// g % 3, then FP16 P_g over its first 32 columns), O at [192, 256).
+constexpr int kSBuffers = 3;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemO = kSBuffers * kStepKeys;
+static_assert(kTmemO + kHeadDim <= kTmemCols, "S buffers and O exceed the TMEM allocation");
 constexpr uint32_t kWaitPolls = 1u << 24;
+constexpr uint32_t kSleepNs = 10000;          // a poll sleeps up to 10 us ...
+constexpr uint32_t kSleepPolls = 1u << 17;    // ... so a wait gives up after about 1.3 s
 constexpr uint32_t kAbortPolls = 1u << 12;  // once the CTA aborts, later waits give up quickly
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // 64^-0.5 * log2(e)
 // P = 2^(s - m + 7) with m the row maximum at its last rescale; m is moved
@@ -137,10 +142,9 @@ struct Barriers {
     uint64_t k_empty[kKStages];  // MMA -> producer: the step's S MMAs completed
     uint64_t v_full[kVStages];   // producer -> MMA: the step's V landed (32 lane arrivals)
     uint64_t v_empty[kVStages];  // MMA -> producer: the step's P.V MMAs completed
-    uint64_t s_full[2];          // MMA -> softmax: S_j in TMEM
-    uint64_t s_empty[2];         // softmax -> MMA: S_j read (4 warp arrivals)
-    uint64_t p_full[2];          // softmax -> MMA: P_j written, O corrected (4 warp arrivals)
-    uint64_t pv_done[2];         // MMA -> softmax: P_j . V_j completed
+    uint64_t s_full[kSBuffers];  // MMA -> softmax: S_g in TMEM
+    uint64_t p_full[kSBuffers];  // softmax -> MMA: P_g in TMEM, O corrected (4 warp arrivals)
+    uint64_t pv_done[kSBuffers]; // MMA -> softmax: P_g . V_g completed (its S buffer is free)
     uint64_t q_full;             // softmax -> MMA: the item's Q tile is in place (4 warp arrivals)
     uint64_t s_drained;          // S issuer -> teardown: every S MMA issued completed
     uint64_t pv_drained;         // P.V issuer -> teardown: every P.V MMA issued completed
@@ -148,10 +152,15 @@ struct Barriers {
 
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t &b) { return pkv::smem_addr(&b); }
 
-// Bounded wait; on a timeout flags the CTA as aborting.
+// Bounded wait; on a timeout flags the CTA as aborting.  Each poll may sleep
+// up to kSleepNs (the thread wakes when the phase completes), so waiting
+// threads do not take issue slots from the softmax by spinning.
 __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort,
                                               int32_t *error_flag) {
-    if (pkv::mbar_wait_bounded(bar, parity, *abort ? kAbortPolls : kWaitPolls)) return true;
+    const uint32_t polls = *abort ? kAbortPolls : kSleepPolls;
+    for (uint32_t i = 0; i < polls; ++i) {
+        if (pkv::mbar_try_wait_sleep(bar, parity, kSleepNs)) return true;
+    }
     atomicOr(error_flag, PKV_DEVICE_WAIT_TIMEOUT);
     *abort = 1;
     return false;
@@ -216,10 +225,8 @@ __global__ void __maxnreg__(120)
 
     const uint32_t raw = pkv::smem_addr(dyn_smem);
     const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-aligned: swizzle atoms
-    uint8_t *const base_ptr = dyn_smem + (base - raw);
     const uint32_t q_smem = base;
-    const uint32_t p_smem = base + kQBytes;                  // P[2]
-    const uint32_t k_smem = base + kQBytes + 2 * kPBytes;     // K ring, 8 KiB a stage
+    const uint32_t k_smem = base + kQBytes;                   // K ring, 8 KiB a stage
     const uint32_t v_smem = k_smem + kKStages * kRingBytes;   // V ring, 8 KiB a stage
 
     const int tiles = (a.tokens + kTileTokens - 1) / kTileTokens;
@@ -246,9 +253,8 @@ __global__ void __maxnreg__(120)
             pkv::mbar_init(bar_addr(bars.v_full[s]), 32);
             pkv::mbar_init(bar_addr(bars.v_empty[s]), 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kSBuffers; ++b) {
             pkv::mbar_init(bar_addr(bars.s_full[b]), 1);
-            pkv::mbar_init(bar_addr(bars.s_empty[b]), kSoftmaxWarps);
             pkv::mbar_init(bar_addr(bars.p_full[b]), kSoftmaxWarps);
             pkv::mbar_init(bar_addr(bars.pv_done[b]), 1);
         }
@@ -351,14 +357,12 @@ __global__ void __maxnreg__(120)
                 if (!wait_or_abort(bar_addr(bars.q_full), round & 1, &abort_flag, a.error_flag)) break;
                 for (int j = 0; j < it.steps; ++j, ++g) {
                     const int st = g % kKStages;
-                    // S_g goes into the S buffer the softmax has read S_{g-2} from,
-                    // once P.V_{g-2} has completed: then s_full(g) also tells the
-                    // softmax that P_{g-2}'s buffer is free for P_g.
+                    // S_g goes into TMEM buffer g % 3 once P.V_{g-3}, which read P_{g-3}
+                    // from it, has completed.
                     if (!wait_or_abort(bar_addr(bars.k_full[st]), (g / kKStages) & 1, &abort_flag, a.error_flag) ||
-                        (g >= 2 && (!wait_or_abort(bar_addr(bars.s_empty[g & 1]), ((g - 2) >> 1) & 1, &abort_flag,
-                                                   a.error_flag) ||
-                                    !wait_or_abort(bar_addr(bars.pv_done[g & 1]), ((g - 2) >> 1) & 1, &abort_flag,
-                                                   a.error_flag)))) {
+                        (g >= kSBuffers &&
+                         !wait_or_abort(bar_addr(bars.pv_done[g % kSBuffers]), ((g - kSBuffers) / kSBuffers) & 1,
+                                        &abort_flag, a.error_flag))) {
                         stop = true;
                         break;
                     }
@@ -366,10 +370,10 @@ __global__ void __maxnreg__(120)
                     const uint64_t k_desc = pkv::tc::desc_k_major_sw128(k_smem + st * kRingBytes);
 #pragma unroll
                     for (int k = 0; k < kHeadDim / 16; ++k) {
-                        pkv::tc::mma_f16_ss(tmem + (g & 1) * kStepKeys, q_desc + 2 * k, k_desc + 2 * k, kIdescS,
+                        pkv::tc::mma_f16_ss(tmem + (g % kSBuffers) * kStepKeys, q_desc + 2 * k, k_desc + 2 * k, kIdescS,
                                             k > 0);
                     }
-                    pkv::tc::commit(bar_addr(bars.s_full[g & 1]));
+                    pkv::tc::commit(bar_addr(bars.s_full[g % kSBuffers]));
                     pkv::tc::commit(bar_addr(bars.k_empty[st]));
                 }
             }
@@ -392,23 +396,25 @@ __global__ void __maxnreg__(120)
                 const Item it = item_info(w, tiles, a);
                 for (int j = 0; j < it.steps; ++j, ++g) {
                     const int st = g % kVStages;
-                    if (!wait_or_abort(bar_addr(bars.p_full[g & 1]), (g >> 1) & 1, &abort_flag, a.error_flag) ||
+                    if (!wait_or_abort(bar_addr(bars.p_full[g % kSBuffers]), (g / kSBuffers) & 1, &abort_flag,
+                                       a.error_flag) ||
                         !wait_or_abort(bar_addr(bars.v_full[st]), (g / kVStages) & 1, &abort_flag, a.error_flag)) {
                         stop = true;
                         break;
                     }
                     pkv::tc::fence_after_sync();
-                    // V boxes are 2 KiB apart (+128 on the descriptor), P's K slices 32 B (+2).
+                    // V boxes are 2 KiB apart (+128 on the descriptor); P's K=16
+                    // slices are 8 TMEM columns apart.
                     const uint64_t v_desc = pkv::tc::desc_mn_major_sw128(v_smem + st * kRingBytes);
-                    const uint64_t p_desc = pkv::tc::desc_k_major_sw128(p_smem + (g & 1) * kPBytes);
+                    const uint32_t p_tmem = tmem + (g % kSBuffers) * kStepKeys;
                     const int nb = min(kStepBlocks, it.nblocks - j * kStepBlocks);
                     for (int kb = 0; kb < nb; ++kb) {
                         // The item's first MMA overwrites O (read out by the softmax
                         // before it published P_g).
-                        pkv::tc::mma_f16_ss(tmem + kTmemO, p_desc + 2 * kb, v_desc + 128 * kb, kIdescO,
+                        pkv::tc::mma_f16_ts(tmem + kTmemO, p_tmem + 8 * kb, v_desc + 128 * kb, kIdescO,
                                             j > 0 || kb > 0);
                     }
-                    pkv::tc::commit(bar_addr(bars.pv_done[g & 1]));
+                    pkv::tc::commit(bar_addr(bars.pv_done[g % kSBuffers]));
                     pkv::tc::commit(bar_addr(bars.v_empty[st]));
                 }
             }
@@ -422,6 +428,7 @@ __global__ void __maxnreg__(120)
         const int r = threadIdx.x;
         const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
         bool ok = true;
+        bool s_ready = false;  // s_full(g) seen complete by a test during step g - 1
         int g = 0;
         // The first item's Q tile; each later one is loaded during the last step
         // of the item before it, once every S MMA that read the tile has completed.
@@ -443,20 +450,19 @@ __global__ void __maxnreg__(120)
             float m = -INFINITY;  // the row maximum at its last rescale (log2 units)
             float l = 0.f;        // sum of this row's weights, relative to m
             for (int j = 0; j < it.steps; ++j, ++g) {
-                const int b = g & 1;
+                const uint32_t sbuf = lanes + (g % kSBuffers) * kStepKeys;  // S_g, then P_g
                 const bool last = j == it.steps - 1;
-                if (!warp_wait(bar_addr(bars.s_full[b]), (g >> 1) & 1, &abort_flag, a.error_flag)) {
+                if (!__all_sync(0xffffffffu, s_ready) &&
+                    !warp_wait(bar_addr(bars.s_full[g % kSBuffers]), (g / kSBuffers) & 1, &abort_flag,
+                               a.error_flag)) {
                     ok = false;
                     break;
                 }
                 pkv::tc::fence_after_sync();
                 uint32_t sr[2][32];
-                pkv::tc::tmem_ld32(lanes + b * kStepKeys, sr[0]);
-                pkv::tc::tmem_ld32(lanes + b * kStepKeys + 32, sr[1]);
+                pkv::tc::tmem_ld32(sbuf, sr[0]);
+                pkv::tc::tmem_ld32(sbuf + 32, sr[1]);
                 pkv::tc::tmem_wait_ld();
-                pkv::tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) pkv::mbar_arrive(bar_addr(bars.s_empty[b]));
                 // s_full of the item's last step: every S MMA of the item has
                 // completed, so the next item's Q may replace this one's.
                 if (last && next < items) load_q_row(q_smem, a, item_info(next, tiles, a), r);
@@ -471,47 +477,51 @@ __global__ void __maxnreg__(120)
                         if (key0 + c > pos) s[c] = -INFINITY;
                     }
                 }
-                // Row maximum over 8 independent chains: one dependent chain of 64
-                // would cost its full latency every step.
+                // Row maximum over 8 independent chains of 3-input maxima: one
+                // dependent chain of 64 would cost its full latency every step.
                 float mx8[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) mx8[e] = s[e];
+                for (int e = 0; e < 8; ++e) mx8[e] = pkv::fmax3(s[e], s[e + 8], s[e + 16]);
 #pragma unroll
-                for (int c = 8; c < 64; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-                const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                for (int e = 0; e < 8; ++e) mx8[e] = pkv::fmax3(mx8[e], s[e + 24], s[e + 32]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx8[e] = pkv::fmax3(mx8[e], s[e + 40], s[e + 48]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) mx8[e] = fmaxf(mx8[e], s[e + 56]);
+                const float mx = pkv::fmax3(pkv::fmax3(mx8[0], mx8[1], mx8[2]), pkv::fmax3(mx8[3], mx8[4], mx8[5]),
+                                            fmaxf(mx8[6], mx8[7]));
                 // Step 0 holds position 0, which every row attends to: m is finite from step 0 on.
                 const float m_blk = mx * kScaleLog2;
                 const float m_new = m_blk > m + kRescaleLog2 ? m_blk : m;  // m = -inf at step 0: always moves
-                // P_g reuses the buffer of P_{g-2}: the S issuer issued S_g only after
-                // P.V_{g-2} had completed, so s_full(g) covered that.
-                // P_g as FP16 (x 2^7) into buffer b, row r, K-major with the 128-byte
-                // swizzle; l sums the FP32 weights over 8 independent chains.
+                // P_g as FP16 (x 2^7) over the first 32 columns of its S buffer,
+                // two keys to a column (the A operand of P.V from TMEM); l sums the
+                // FP32 weights over 8 independent chains.
                 const float shift = kWeightShift - m_new;
-                uint8_t *prow = base_ptr + (p_smem - base) + b * kPBytes + (r >> 3) * 1024 + (r & 7) * kRowBytes;
                 float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int c8 = 0; c8 < 8; ++c8) {
-                    __half2 h[4];
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t pr[16];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float lo = pkv::exp2_approx(fmaf(s[8 * c8 + 2 * e], kScaleLog2, shift));
-                        const float hi = pkv::exp2_approx(fmaf(s[8 * c8 + 2 * e + 1], kScaleLog2, shift));
-                        l8[2 * e] += lo;
-                        l8[2 * e + 1] += hi;
-                        h[e] = __floats2half2_rn(lo, hi);
+                    for (int c = 0; c < 16; ++c) {
+                        const int k = 32 * half + 2 * c;
+                        const float lo = pkv::exp2_approx(fmaf(s[k], kScaleLog2, shift));
+                        const float hi = pkv::exp2_approx(fmaf(s[k + 1], kScaleLog2, shift));
+                        l8[k & 7] += lo;
+                        l8[(k + 1) & 7] += hi;
+                        pr[c] = pkv::pack_half2(__floats2half2_rn(lo, hi));
                     }
-                    *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) =
-                        make_uint4(pkv::pack_half2(h[0]), pkv::pack_half2(h[1]), pkv::pack_half2(h[2]),
-                                   pkv::pack_half2(h[3]));
+                    pkv::tc::tmem_st16(sbuf + 16 * half, pr);
                 }
+                // Test s_full(g + 1) now: its answer is needed only at the next
+                // step, so the test's latency overlaps this step's work.
+                s_ready = pkv::mbar_test_wait(bar_addr(bars.s_full[(g + 1) % kSBuffers]), ((g + 1) / kSBuffers) & 1);
                 const float corr = m_new != m ? pkv::exp2_approx(m - m_new) : 1.f;  // 0 at step 0, where l is 0
                 l = l * corr + (((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7])));
                 if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
                     // Some row's reference maximum moved: rescale its O (scaled by the
                     // old one so far) once P_{g-1} . V_{g-1} is in it, before
                     // P_g . V_g adds to it.
-                    if (!warp_wait(bar_addr(bars.pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, &abort_flag,
+                    if (!warp_wait(bar_addr(bars.pv_done[(g - 1) % kSBuffers]), ((g - 1) / kSBuffers) & 1, &abort_flag,
                                    a.error_flag)) {
                         ok = false;
                         break;
@@ -527,21 +537,22 @@ __global__ void __maxnreg__(120)
                         for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * corr);
                         pkv::tc::tmem_st32(taddr, o);
                     }
-                    pkv::tc::tmem_wait_st();
                 }
+                pkv::tc::tmem_wait_st();  // P_g (and a rescaled O) written
                 m = m_new;
                 if (last && next < items) pkv::cp_async_wait<0>();  // the next item's Q row landed
-                pkv::fence_proxy_async_smem();  // P_g (and that Q row) -> the MMA's reads
+                pkv::fence_proxy_async_smem();  // that Q row -> the MMA's (async proxy) reads
                 pkv::tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) {
-                    pkv::mbar_arrive(bar_addr(bars.p_full[b]));
+                    pkv::mbar_arrive(bar_addr(bars.p_full[g % kSBuffers]));
                     if (last && next < items) pkv::mbar_arrive(bar_addr(bars.q_full));
                 }
             }
             if (!ok) break;
             // The item's output: O / l once its last P.V has completed.
-            if (!warp_wait(bar_addr(bars.pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, &abort_flag, a.error_flag)) {
+            if (!warp_wait(bar_addr(bars.pv_done[(g - 1) % kSBuffers]), ((g - 1) / kSBuffers) & 1, &abort_flag,
+                           a.error_flag)) {
                 break;
             }
             pkv::tc::fence_after_sync();
