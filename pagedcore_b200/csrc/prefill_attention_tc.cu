@@ -26,28 +26,32 @@
 //   the pool are zero-filled, so 0 * NaN never reaches a sum.  A step is
 //   published after the copies of the step 2 (K) or 1 (V) ahead have been
 //   issued and its own have landed (cp.async.wait_group, a proxy fence, an
-//   mbarrier arrival per lane).  Copies of 2 KiB boxes issued by one thread
-//   through the tensor-memory-access unit issued far slower than these.
+//   mbarrier arrival per lane).  (TMA loads of the same 2 KiB boxes from one
+//   issuing thread measured slower.)
 // - warps 5 and 7 (one thread each; warp 5 owns the TMEM allocation): the
 //   MMA issuers.  Warp 5 issues S_g = Q . K_g^T (M 128, N 64, K 64: four K=16
-//   MMAs) into TMEM S buffer g % 2 once K_g has landed, the softmax has read
-//   S_{g-2} and P.V_{g-2} has completed (so s_full(g) also frees P_{g-2}'s
-//   shared-memory buffer for P_g); warp 7 issues O += P_g . V_g (M 128, N 64,
-//   one K=16 MMA per block) into the TMEM O once P_g is written.  Two issuing
-//   threads: an MMA and every mbarrier wait take hundreds of cycles, and the
-//   two streams are independent.
+//   MMAs) into TMEM S buffer g % 3 once K_g has landed and P.V_{g-3}, which
+//   read P_{g-3} from that buffer, has completed; warp 7 issues
+//   O += P_g . V_g (M 128, N 64, one K=16 MMA per block) with P_g read from
+//   TMEM (the A operand) and V_g from shared memory, into the TMEM O.  Two
+//   issuing threads: an MMA and every mbarrier wait take hundreds of cycles,
+//   and the two streams are independent.
 // - warps 0-3 (128 threads, thread r = row r, TMEM lane r): the softmax.  A
 //   thread reads its row of S_g from TMEM (tcgen05.ld), masks positions past
 //   its token, and keeps the online softmax state in base 2 in FP32: a
 //   reference maximum m that moves only when the row's maximum passes it by
-//   more than 2^8.  It writes P_g = 2^(s - m + 7) (<= 2^15) as FP16 into
-//   shared memory in the MMA's K-major swizzled layout, and sums the FP32
-//   weights into the normaliser l.  When m moves, the thread rescales its row
-//   of O in TMEM (ld, multiply, st) once the previous P.V has completed, and l
-//   in registers.  At the end of an item O * (1 / l) is rounded to FP16.  The
-//   softmax threads also load each item's Q tile (cp.async): the first at
-//   start-up, each later one during the last step of the item before it, once
-//   s_full shows that every S MMA reading the old tile has completed.
+//   more than 2^8.  It writes P_g = 2^(s - m + 7) (<= 2^15) as FP16 over the
+//   first 32 columns of S_g's buffer (tcgen05.st, two keys to a column), and
+//   sums the FP32 weights into the normaliser l.  When m moves, the thread
+//   rescales its row of O in TMEM (ld, multiply, st) once the previous P.V has
+//   completed, and l in registers.  At the end of an item O * (1 / l) is
+//   rounded to FP16.  The softmax threads also load each item's Q tile
+//   (cp.async): the first at start-up, each later one during the last step of
+//   the item before it, once s_full shows that every S MMA reading the old
+//   tile has completed.
+//
+// TMEM: S/P buffers at columns 0, 64, 128, O at 192 (256 columns, two CTAs
+// per SM).  Shared memory: Q (16 KiB) and the K and V rings.
 //
 // Block ids outside the pool set PKV_DEVICE_BAD_BLOCK and read as zeros.
 // Every wait is bounded: on a timeout the thread sets

@@ -79,8 +79,9 @@ def test_prefill_attention_matches_the_oracle_for_every_token(chunks) -> None:
     allocator.check_device_errors()
 
 
-# (300, 1200): a chunk long enough for whole 16-token tiles that continues a
-# cache (start 300 shifts the diagonal block and every tile's block count).
+# (300, 1200): a long chunk that continues a cache (start 300 shifts the
+# diagonal block and every tile's block count); at these lengths each
+# persistent CTA walks more than one (tile, head) item.
 @pytest.mark.parametrize("chunks", [(2047,), (1000, 1048), (300, 1200)])
 def test_prefill_attention_at_the_full_context(chunks) -> None:
     device = cuda_device()
