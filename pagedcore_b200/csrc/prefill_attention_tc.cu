@@ -544,8 +544,10 @@ __global__ void __maxnreg__(120)
                 }
                 pkv::tc::tmem_wait_st();  // P_g (and a rescaled O) written
                 m = m_new;
-                if (last && next < items) pkv::cp_async_wait<0>();  // the next item's Q row landed
-                pkv::fence_proxy_async_smem();  // that Q row -> the MMA's (async proxy) reads
+                if (last && next < items) {
+                    pkv::cp_async_wait<0>();         // the next item's Q row landed
+                    pkv::fence_proxy_async_smem();   // and is ordered before the MMA's (async proxy) reads
+                }
                 pkv::tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) {
