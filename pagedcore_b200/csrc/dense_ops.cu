@@ -306,7 +306,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __half *__r
                                                                __half *__restrict__ y, int64_t y_stride) {
     const int lane = threadIdx.x & 31;
     const int chunks = k / kChunk;
-    for (int n = blockIdx.x * kGemvWarps + (threadIdx.x >> 5); n < n_rows; n += gridDim.x * kGemvWarps) {
+    // Launched as a programmatic dependent: the weight does not depend on the
+    // previous kernel, so the warp's first row is brought into L2 before the
+    // wait for that kernel (which wrote x); x and y only after it.
+    pkv::pdl_launch_dependents();
+    const int first = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+    if (first < n_rows) {
+        for (int c = lane; c < chunks; c += 32) pkv::prefetch_l2(w + static_cast<int64_t>(first) * k + c * kChunk);
+    }
+    pkv::pdl_wait();
+    for (int n = first; n < n_rows; n += gridDim.x * kGemvWarps) {
         const __half *row = w + static_cast<int64_t>(n) * k;
         float acc[M];
 #pragma unroll
@@ -346,8 +355,8 @@ template <int M>
 cudaError_t launch_gemv(const __half *x, int64_t x_stride, const __half *w, int n, int k, __half *y,
                         int64_t y_stride, cudaStream_t stream) {
     const int grid = (n + kGemvWarps - 1) / kGemvWarps;
-    gemv_kernel<M><<<grid, kGemvWarps * 32, 0, stream>>>(x, x_stride, w, n, k, y, y_stride);
-    return cudaGetLastError();
+    return pkv::launch_pdl(gemv_kernel<M>, dim3(grid), dim3(kGemvWarps * 32), stream, x, x_stride, w, n, k, y,
+                           y_stride);
 }
 
 }  // namespace
