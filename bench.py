@@ -1208,7 +1208,7 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
     with RoPE, causal prefill attention over the block table, output
     projection, norm, gate/up GEMM, SwiGLU product, down projection), final
     norm and LM head for every prompt token.  The roofline is the hand-written
-    attention kernel's (``prefill_attention_kernel``), timed alone over the
+    attention kernel's (``prefill_tc_kernel``), timed alone over the
     same chunk on the same stream: its algorithmic MMA work over the measured
     dense tensor peak.
     """
