@@ -500,21 +500,32 @@ __global__ void __maxnreg__(120)
                 // P_g as FP16 (x 2^7) over the first 32 columns of its S buffer,
                 // two keys to a column (the A operand of P.V from TMEM); l sums the
                 // FP32 weights over 8 independent chains.
+                // Pairs of keys go through the packed FP32 instructions (the same
+                // rounding as two scalar ones, half the instructions).
                 const float shift = kWeightShift - m_new;
-                float l8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                const uint64_t scale2 = pkv::f32x2(kScaleLog2, kScaleLog2);
+                const uint64_t shift2 = pkv::f32x2(shift, shift);
+                uint64_t l4[4] = {0, 0, 0, 0};  // FP32 pairs: 8 independent chains
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     uint32_t pr[16];
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
                         const int k = 32 * half + 2 * c;
-                        const float lo = pkv::exp2_approx(fmaf(s[k], kScaleLog2, shift));
-                        const float hi = pkv::exp2_approx(fmaf(s[k + 1], kScaleLog2, shift));
-                        l8[k & 7] += lo;
-                        l8[(k + 1) & 7] += hi;
+                        const float2 x = pkv::unpack_f32x2(pkv::fma_f32x2(pkv::f32x2(s[k], s[k + 1]), scale2, shift2));
+                        const float lo = pkv::exp2_approx(x.x);
+                        const float hi = pkv::exp2_approx(x.y);
+                        l4[c & 3] = pkv::add_f32x2(l4[c & 3], pkv::f32x2(lo, hi));
                         pr[c] = pkv::pack_half2(__floats2half2_rn(lo, hi));
                     }
                     pkv::tc::tmem_st16(sbuf + 16 * half, pr);
+                }
+                float l8[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 v = pkv::unpack_f32x2(l4[e]);
+                    l8[2 * e] = v.x;
+                    l8[2 * e + 1] = v.y;
                 }
                 // Test s_full(g + 1) now: its answer is needed only at the next
                 // step, so the test's latency overlaps this step's work.
