@@ -41,7 +41,7 @@ LAYERS = 22
 CALIBRATION_STEPS = 8  # staged steps in which KVAllocator(balance="measured") learns its piece weights
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_TENSOR_TFLOPS = 1590.0
-PREFILL_DRAM_BYTES_2047 = 10_530_560  # prefill_tc_kernel, one launch, ncu (read 10.53 MB, write 0)
+PREFILL_DRAM_BYTES_2047 = 10_529_280  # prefill_tc_kernel, one launch, ncu (read 10.53 MB, write 0)
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one fused
 # decode-layer launch over its algorithmic bytes, from one capture of the
 # config 4 step; the committed ncu summary of decode_kernel gives the command.
