@@ -958,7 +958,10 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
         allocator.append(request, kv, kv, rotate=True)
     weights = random_weights(seed, device, generator_device=device)
     decoder = BatchedDecoder(weights)
-    exchange = StepExchange(wait=timedelta(seconds=120)) if world > 1 else None
+    # Peers are checked in the store every 16th step (a rank's failure is then
+    # noticed within 16 steps, or by the process group's timeout): a store
+    # round trip per step would hold every host back to the slowest rank's.
+    exchange = StepExchange(wait=timedelta(seconds=120), check_every=16) if world > 1 else None
     sharded = ShardedGreedyDecoder(decoder, allocator, batch, exchange)
     first = torch.randint(0, 32000, (rows, 1), device=device, generator=generator)
     stream = torch.cuda.current_stream(device)
@@ -1050,7 +1053,7 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
                     "gathered tokens of the whole batch read back and waited for every step",
         },
         "token_gather": ("NCCL all_gather_into_tensor of int64 next-token ids every step "
-                         f"({rows * world * 8} B gathered), peers checked in the store every step")
+                         f"({rows * world * 8} B gathered), peers checked in the store every 16th step")
         if world > 1 else "none at N = 1 (one rank holds the whole batch)",
         "roofline": {
             "bound": "hbm",
