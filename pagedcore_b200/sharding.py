@@ -73,6 +73,7 @@ class StepExchange:
         self.wait = wait
         self.check_every = check_every
         self.step = 0
+        self._buffers: dict = {}
 
     # -- failure marks ---------------------------------------------------------
     def fail(self, error: BaseException | str) -> None:
@@ -119,13 +120,21 @@ class StepExchange:
         if self.step % self.check_every == 0:
             self._await_peers()
         per_rank = -(-count // self.world)
-        padded = torch.full((per_rank,), -1, dtype=torch.int64, device=local.device)
+        # The collective's buffers are kept from step to step (same addresses
+        # every step), each step's result is returned as a copy.
+        key = (count, local.device)
+        if self._buffers.get("key") != key:
+            self._buffers = {
+                "key": key,
+                "padded": torch.full((per_rank,), -1, dtype=torch.int64, device=local.device),
+                "gathered": torch.empty(self.world * per_rank, dtype=torch.int64, device=local.device),
+            }
+        padded, gathered = self._buffers["padded"], self._buffers["gathered"]
         padded[:owned] = local
-        gathered = torch.empty(self.world * per_rank, dtype=torch.int64, device=local.device)
         dist.all_gather_into_tensor(gathered, padded, group=self.group)
         self.step += 1
         # Rank r's j-th id belongs to batch position r + j*world.
-        return gathered.view(self.world, per_rank).t().reshape(-1)[:count]
+        return gathered.view(self.world, per_rank).t().reshape(-1)[:count].clone()
 
 
 class ShardedGreedyDecoder:
