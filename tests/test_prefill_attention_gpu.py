@@ -81,8 +81,9 @@ def test_prefill_attention_matches_the_oracle_for_every_token(chunks) -> None:
 
 # (300, 1200): a long chunk that continues a cache (start 300 shifts the
 # diagonal block and every tile's block count); at these lengths each
-# persistent CTA walks more than one (tile, head) item.
-@pytest.mark.parametrize("chunks", [(2047,), (1000, 1048), (300, 1200)])
+# persistent CTA walks more than one (tile, head) item.  (2000, 47): a short
+# chunk at the end of a full cache, few items that each walk every block.
+@pytest.mark.parametrize("chunks", [(2047,), (1000, 1048), (300, 1200), (2000, 47)])
 def test_prefill_attention_at_the_full_context(chunks) -> None:
     device = cuda_device()
     allocator = fragmented_allocator(128, 5, device)
