@@ -465,8 +465,9 @@ GEMV_MAX_ROWS = 1
 # Rows up to which ``linear`` uses the tcgen05 split-K kernel.  The kernel
 # takes up to 256 rows (its MMA N limit); measured on B200 over 22 layers of the
 # decoder step's projections, norms and SwiGLU product replayed as one graph,
-# it beats the library GEMM up to 32 rows (37.7 against 40.1 us per layer at
-# 32) and falls behind from 64 rows (51 against 41 at 64, 69 against 47 at 256).
+# it is ahead of the library GEMM at 8 rows (39.8 against 46.1 us per layer),
+# even with it at 16-32 (40.4 against 39.5, 40.3 against 40.1) and behind from
+# 64 rows (46 against 41 at 64, 69 against 47 at 256).
 TC_MAX_ROWS = 32
 
 _linear_errors: dict[int, Tensor] = {}
