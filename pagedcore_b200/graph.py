@@ -23,7 +23,9 @@ ledger records the 22 layers after each replay is enqueued.
 
 from __future__ import annotations
 
-from collections.abc import Sequence
+import contextlib
+import gc
+from collections.abc import Iterator, Sequence
 
 import torch
 from torch import Tensor
@@ -34,6 +36,28 @@ from pagedcore_b200.engine_types import RequestId
 from pagedcore_b200.kv_cache import KVAllocator
 
 _LAYERS = 22
+
+
+@contextlib.contextmanager
+def _capturing(graph: torch.cuda.CUDAGraph, stream: torch.cuda.Stream) -> Iterator[None]:
+    """Capture into ``graph`` on ``stream`` with the cycle collector held off.
+
+    A CUDA graph that its last user left in a reference cycle is destroyed
+    whenever the collector runs; if that happens mid-capture, the destroy
+    is a call CUDA forbids while this thread captures, and the capture is
+    lost.  So dead cycles are collected first and the collector waits until
+    the capture has ended.  The capture is thread-local: another thread's
+    CUDA queries (a communication library's watchdog, say) cannot spoil it.
+    """
+    gc.collect()
+    enabled = gc.isenabled()
+    gc.disable()
+    try:
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+            yield
+    finally:
+        if enabled:
+            gc.enable()
 
 
 def _replay_args(allocator: KVAllocator, rows: int, grid: int) -> tuple:
@@ -97,7 +121,7 @@ class DecodeStepGraph:
         side = torch.cuda.Stream(allocator.pool.device)
         side.wait_stream(allocator._stream)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
+        with _capturing(graph, side):
             for layer in range(_LAYERS):
                 q, k, v, o = query[layer], key[layer], value[layer], out[layer]
                 check(
@@ -200,7 +224,7 @@ class DecoderStepGraph:
         with torch.cuda.stream(side):
             self.decoder.forward(self.ids, lambda layer, q, k, v: out)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
+        with _capturing(graph, side):
             logits = self.decoder.forward(self.ids, attend)
         allocator._stream.wait_stream(side)
         self.captures += 1

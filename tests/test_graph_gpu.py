@@ -7,13 +7,15 @@ over steps that alternate the upload buffers and the caller's buffer sets.
 
 from __future__ import annotations
 
+import gc
+
 import numpy as np
 import pytest
 import torch
 
 from pagedcore_b200 import workloads
 from pagedcore_b200.engine_types import KVReservation, RequestId
-from pagedcore_b200.graph import DecodeStepGraph
+from pagedcore_b200.graph import DecodeStepGraph, _capturing
 from pagedcore_b200.kv_cache import KVAllocator
 from tests.conftest import cuda_device
 
@@ -109,3 +111,36 @@ def test_graph_step_rejects_buffers_of_the_wrong_shape() -> None:
     with pytest.raises(ValueError, match="key must be"):
         engine.step(q, kv[:, :1], kv, torch.empty_like(q))
     assert [allocator.cached_length(r) for r in requests] == [5, 30]
+
+
+def test_a_graph_dropped_in_a_reference_cycle_mid_capture_does_not_spoil_it() -> None:
+    """A CUDA graph left in a reference cycle is destroyed when the cycle
+    collector runs.  Dropped during a capture, with a collection due at every
+    allocation, it must wait: destroying it mid-capture would lose the
+    capture.  The capture then replays, and the old graph is freed once the
+    capture has ended."""
+    device = cuda_device()
+    x = torch.ones(4, device=device)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    old = torch.cuda.CUDAGraph()
+    with _capturing(old, side):
+        x.add_(1)
+    threshold = gc.get_threshold()
+    graph = torch.cuda.CUDAGraph()
+    try:
+        gc.set_threshold(1, 1, 1)
+        with _capturing(graph, side):
+            x.mul_(3)
+            cycle = [old]
+            cycle.append(cycle)
+            del old, cycle
+            kept = [[] for _ in range(1000)]  # each list kept makes a collection due
+            del kept
+    finally:
+        gc.set_threshold(*threshold)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph.replay()  # captured work is not run at capture: x goes from 1 to 3
+    torch.cuda.synchronize(device)
+    assert x.tolist() == [3.0] * 4
+    gc.collect()  # the old graph, never replayed, is freed outside any capture
