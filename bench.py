@@ -234,8 +234,8 @@ def _nvml_handle(pynvml, device: int):
     return pynvml.nvmlDeviceGetHandleByIndex(device)
 
 
-def _sample_clocks(bus_id: str | None, index: int, period: float, ready, stop, sink) -> None:
-    """Child process: NVML SM clock and throttle reasons every `period` s until `stop`."""
+def _sample_clocks(bus_id: str | None, index: int, period: float, ready, recording, stop, sink) -> None:
+    """Child process: NVML SM clock and throttle reasons every `period` s while `recording`, until `stop`."""
     samples, max_mhz, error = [], None, None
     try:
         import pynvml
@@ -251,9 +251,10 @@ def _sample_clocks(bus_id: str | None, index: int, period: float, ready, stop, s
         pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
         ready.set()
         while not stop.is_set():
-            samples.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
-                            int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
-            stop.wait(period)
+            if recording.wait(period):
+                samples.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
+                                int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+                stop.wait(period)
     except Exception as exc:  # noqa: BLE001 - clocks are reported, never required
         error = f"NVML unavailable: {exc}"
         ready.set()
@@ -264,7 +265,10 @@ class ClockSampler:
     """SM clock and throttle-reason samples (NVML, read-only) every 2 ms of the timed region.
 
     Sampled in a separate (spawned) process, so the sampling never competes
-    with the launching thread for the interpreter lock.
+    with the launching thread for the interpreter lock.  The process starts
+    (about 0.15 s, the GPU idle) when the context is entered, which a leg does
+    before its warm-up, so the timed steps follow the warm-up without a gap;
+    only samples between ``begin()`` and ``end()`` (the timed regions) are kept.
     """
 
     # NVML clock-event reason bits.
@@ -288,18 +292,30 @@ class ClockSampler:
         bus_id = None if bus is None else (f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:"
                                            f"{getattr(props, 'pci_device_id', 0):02x}.0")
         ctx = mp.get_context("spawn")
-        self._ready, self._stop = ctx.Event(), ctx.Event()
+        self._ready, self._recording, self._stop = ctx.Event(), ctx.Event(), ctx.Event()
         self._receive, send = ctx.Pipe(duplex=False)
         self._child = ctx.Process(target=_sample_clocks,
-                                  args=(bus_id, self.device, self.PERIOD, self._ready, self._stop, send), daemon=True)
+                                  args=(bus_id, self.device, self.PERIOD, self._ready, self._recording, self._stop,
+                                        send), daemon=True)
         self._child.start()
         if not self._ready.wait(timeout=120):
             self.error = "clock sampler did not start"
         return self
 
+    def begin(self) -> None:
+        """A timed region starts: keep samples from now on."""
+        if self._child is not None:
+            self._recording.set()
+
+    def end(self) -> None:
+        """The timed region has ended (after its closing synchronisation)."""
+        if self._child is not None:
+            self._recording.clear()
+
     def __exit__(self, *exc) -> None:
         if self._child is None:
             return
+        self._recording.clear()
         self._stop.set()
         if self._receive.poll(30):
             self.samples, self.max_mhz, error = self._receive.recv()
@@ -395,48 +411,50 @@ def kv_leg(args: argparse.Namespace, device, rank: int, world: int, local_rank: 
         torch.cuda.synchronize(device)
 
     # Setup, untimed: the allocator learns each CTA slot's speed over its first
-    # staged steps and then freezes the piece weights.
-    for i in range(CALIBRATION_STEPS):
-        step(*device_inputs[i % 2])
-    for i in range(args.warmup):
-        step(*device_inputs[i % 2])
-    allocator.check_device_errors()
-
-    # Algorithmic bytes of one fused decode-layer launch, from the staged
-    # batch: K/V streamed (1024 B per cached token, the new one included),
-    # block-table entries, Q in / attention out (4 KiB each), the new token's
-    # K/V in (1 KiB) and written to the pool (1 KiB), lengths and prefix.  The
-    # split partials are not counted: they are a by-product of the split, not
-    # bytes the operation needs.
-    plan_info = {}
-
-    def layer_bytes() -> float:
-        with allocator.append_decode(requests):
-            batch = allocator.staged_decode_batch()
-            for layer in range(LAYERS):
-                allocator.decode_layer(layer, *(x[layer] for x in device_inputs[0]), out=out[layer])
-        big, tail = batch.plan.pieces()
-        plan_info.update(grid=batch.plan.grid, blocks_per_cta=batch.plan.blocks_per_cta, big_ctas=big,
-                         tail_blocks=tail, total_blocks=batch.total_blocks)
-        lengths = batch.host_lengths.astype(np.int64)
-        blocks = (lengths + 15) // 16
-        per_row = 1024 * lengths + 4 * blocks + 2 * 4096 + 2 * 1024 + 8
-        return float(per_row.sum())
-
-    # One extra staged step (its tokens are real appends) measures the plan.
-    layer_bytes_per_launch = layer_bytes()
-
-    # No events inside the timed region: an event recorded between two layer
-    # launches delays the next launch by several microseconds, so the layer
-    # time below is the timed region's time over its 22 * K layer launches
-    # (split + combine + the gaps between them, plus each step's table upload).
-    # The timed region is repeated `repeats` times, each exactly `steps` steps
-    # bracketed by a barrier and a device synchronisation; `value` is the
-    # median region, the others give the spread.
-    regions = []
+    # staged steps and then freezes the piece weights.  The clock sampler starts
+    # first, so the timed regions follow the warm-up without an idle gap.
     with ClockSampler(local_rank) as clocks:
+        for i in range(CALIBRATION_STEPS):
+            step(*device_inputs[i % 2])
+        for i in range(args.warmup):
+            step(*device_inputs[i % 2])
+        allocator.check_device_errors()
+
+        # Algorithmic bytes of one fused decode-layer launch, from the staged
+        # batch: K/V streamed (1024 B per cached token, the new one included),
+        # block-table entries, Q in / attention out (4 KiB each), the new token's
+        # K/V in (1 KiB) and written to the pool (1 KiB), lengths and prefix.  The
+        # split partials are not counted: they are a by-product of the split, not
+        # bytes the operation needs.
+        plan_info = {}
+
+        def layer_bytes() -> float:
+            with allocator.append_decode(requests):
+                batch = allocator.staged_decode_batch()
+                for layer in range(LAYERS):
+                    allocator.decode_layer(layer, *(x[layer] for x in device_inputs[0]), out=out[layer])
+            big, tail = batch.plan.pieces()
+            plan_info.update(grid=batch.plan.grid, blocks_per_cta=batch.plan.blocks_per_cta, big_ctas=big,
+                             tail_blocks=tail, total_blocks=batch.total_blocks)
+            lengths = batch.host_lengths.astype(np.int64)
+            blocks = (lengths + 15) // 16
+            per_row = 1024 * lengths + 4 * blocks + 2 * 4096 + 2 * 1024 + 8
+            return float(per_row.sum())
+
+        # One extra staged step (its tokens are real appends) measures the plan.
+        layer_bytes_per_launch = layer_bytes()
+
+        # No events inside the timed region: an event recorded between two layer
+        # launches delays the next launch by several microseconds, so the layer
+        # time below is the timed region's time over its 22 * K layer launches
+        # (split + combine + the gaps between them, plus each step's table upload).
+        # The timed region is repeated `repeats` times, each exactly `steps` steps
+        # bracketed by a barrier and a device synchronisation; `value` is the
+        # median region, the others give the spread.
+        regions = []
         for _ in range(repeats):
             barrier()
+            clocks.begin()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.nvtx.range_push("timed")
             start.record(stream)
@@ -445,6 +463,7 @@ def kv_leg(args: argparse.Namespace, device, rank: int, world: int, local_rank: 
             end.record(stream)
             torch.cuda.nvtx.range_pop()
             barrier()
+            clocks.end()
             regions.append(start.elapsed_time(end))
     allocator.check_device_errors()
 
@@ -669,9 +688,11 @@ def run_stress_arm(args: argparse.Namespace) -> None:
     run = StressRun(device, seed=5 + 1000 * rank)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
-    run.warm(args.stress_warmup)
     with ClockSampler(local_rank) as clocks:
+        run.warm(args.stress_warmup)
+        clocks.begin()
         result = run.run(0, args.stress_iterations)
+        clocks.end()
     totals = torch.tensor([result.seconds, result.decode_tokens, result.attention_bytes], dtype=torch.float64,
                           device=device)
     if world > 1:
@@ -787,13 +808,14 @@ def run_append_arm(args: argparse.Namespace) -> None:
         kernels.append_kv(pool, key, value, slots_device, layer_begin=0, error_flag=allocator._error,
                           positions=positions_device, rope_table=allocator._rope)
 
-    for _ in range(args.warmup):
-        kernel_step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        for _ in range(args.warmup):
+            kernel_step()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.begin()
         torch.cuda.nvtx.range_push("timed")
         start.record(stream)
         for _ in range(args.steps):
@@ -801,6 +823,7 @@ def run_append_arm(args: argparse.Namespace) -> None:
         end.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
+        clocks.end()
     kernel_ms = start.elapsed_time(end) / args.steps
     allocator.check_device_errors()
 
@@ -971,12 +994,13 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(device)
 
-    ids = first
-    for _ in range(CALIBRATION_STEPS + args.warmup):
-        ids, gathered = sharded.step(ids)
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        ids = first
+        for _ in range(CALIBRATION_STEPS + args.warmup):
+            ids, gathered = sharded.step(ids)
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.begin()
         torch.cuda.nvtx.range_push("timed")  # marks the timed launches for an ncu launch list
         start.record(stream)
         for _ in range(args.steps):
@@ -984,6 +1008,7 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
         end.record(stream)
         torch.cuda.nvtx.range_pop()
         barrier()
+        clocks.end()
     step_ms = start.elapsed_time(end) / args.steps
     allocator.check_device_errors()
 
@@ -1257,12 +1282,13 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    for _ in range(args.warmup):
-        prefill(ids)
-    torch.cuda.synchronize(device)
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        for _ in range(args.warmup):
+            prefill(ids)
+        torch.cuda.synchronize(device)
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.begin()
         torch.cuda.nvtx.range_push("timed")  # marks the timed launches for an ncu launch list
         start.record(stream)
         for _ in range(args.steps):
@@ -1270,6 +1296,7 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
         end.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize(device)
+        clocks.end()
     step_ms = start.elapsed_time(end) / args.steps
     # End to end through the public call: the prompt ids copied from pinned
     # host memory and the last token's logits read back, every step.

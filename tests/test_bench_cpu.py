@@ -33,3 +33,46 @@ def test_prefill_cpu_baseline_times_the_dense_prefill_on_a_sample() -> None:
     assert line["unit"] == "tokens/s" and line["kind"] == "port"
     assert line["value"] > 0 and line["cores"] == torch.get_num_threads()
     assert "first 16 tokens" in line["sample"]
+
+
+def test_clock_samples_are_kept_only_inside_the_timed_window(monkeypatch) -> None:
+    """The sampler runs from before the warm-up; only samples taken between
+    begin() and end() (the recording event) reach the report.  A fake NVML
+    reports 1965 MHz inside the window and 100 MHz outside it."""
+    import sys
+    import threading
+    import time
+    import types
+
+    clock = [100.0]
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=0,
+        NVMLError=Exception,
+        nvmlInit=lambda: None,
+        nvmlDeviceGetHandleByPciBusId=lambda bus: "gpu",
+        nvmlDeviceGetHandleByIndex=lambda index: "gpu",
+        nvmlDeviceGetMaxClockInfo=lambda handle, kind: 1965,
+        nvmlDeviceGetClockInfo=lambda handle, kind: clock[0],
+        nvmlDeviceGetCurrentClocksEventReasons=lambda handle: 0x4,
+    )
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    ready, recording, stop = threading.Event(), threading.Event(), threading.Event()
+    sent = []
+    sink = types.SimpleNamespace(send=sent.append)
+    worker = threading.Thread(target=bench._sample_clocks,
+                              args=("00000000:01:00.0", 0, 0.001, ready, recording, stop, sink))
+    worker.start()
+    assert ready.wait(5)
+    time.sleep(0.05)  # the warm-up: not kept
+    clock[0] = 1965.0
+    recording.set()
+    time.sleep(0.05)  # the timed region
+    recording.clear()
+    time.sleep(0.02)  # a read in flight at the clear finishes first
+    clock[0] = 100.0
+    time.sleep(0.05)
+    stop.set()
+    worker.join(5)
+    samples, max_mhz, error = sent[0]
+    assert error is None and max_mhz == 1965.0
+    assert samples and all(mhz == 1965.0 and bits == 0x4 for mhz, bits in samples)
