@@ -1057,11 +1057,7 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
     step_bytes = weight_bytes + kv_bytes + rows * 2048 * 2
     peak, peak_kind = _peak_hbm()
     achieved = step_bytes / (step_ms / 1000.0) / 1e9
-    # This library's kernels per step: per layer the two fused residual-add
-    # norms, the decode layer's split and combine launches and the SwiGLU
-    # product, then the final norm.  GEMMs, embedding and argmax are library
-    # kernels; so is the NCCL gather.
-    launches = LAYERS * 5 + 1
+    launches = _step_launches(rows)
     return {
         "value": world * rows / (step_ms / 1000.0),
         "unit": "tokens/s",
@@ -1096,6 +1092,32 @@ def decoder_leg(args: argparse.Namespace, device, rank: int, world: int, local_r
         "gpu_launches": args.steps * launches,
         "clocks": clocks.summary(),
     }
+
+
+def _step_launches(rows: int) -> int:
+    """This library's kernel launches in one pass of ``BatchedDecoder.forward`` over ``rows`` rows.
+
+    Per layer five: the two fused residual-add norms, the SwiGLU product and
+    the attention's two (a decode step: the decode layer's split and combine;
+    a prefill: the K/V write and the causal attention), then the final norm.
+    The projections follow ``kernels.linear``'s routing: one row runs this
+    library's matrix-vector kernel (four per layer and the LM head), 2 to
+    ``TC_MAX_ROWS`` rows its tcgen05 linear layer (the same five launches, plus
+    a split-sum launch where the fused Q/K/V or the LM head is split over K;
+    the other splits are added by the fused norm and SwiGLU kernels), more
+    rows the library GEMM.  Embedding, argmax and the NCCL gather are library
+    kernels.
+    """
+    from pagedcore_b200 import kernels
+
+    launches = LAYERS * 5 + 1
+    if rows <= kernels.GEMV_MAX_ROWS:
+        launches += 4 * LAYERS + 1
+    elif rows <= kernels.TC_MAX_ROWS:
+        launches += 4 * LAYERS + 1
+        launches += LAYERS * (kernels.linear_splits(rows, 2560, 2048) > 1)
+        launches += kernels.linear_splits(rows, 32000, 2048) > 1
+    return launches
 
 
 def run_decoder_arm(args: argparse.Namespace) -> None:
@@ -1243,7 +1265,6 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
 
-    from pagedcore_b200 import kernels
     from pagedcore_b200.decoder import BatchedDecoder
     from pagedcore_b200.engine_types import KVReservation, RequestId
     from pagedcore_b200.kv_cache import KVAllocator
@@ -1385,7 +1406,7 @@ def run_prefill_arm(args: argparse.Namespace) -> None:
             # the final norm.  The GEMMs and the embedding are library/torch kernels,
             # except that a one-token prompt's projections (Q/K/V, o, gate/up, down per
             # layer and the LM head) run this library's matrix-vector kernel.
-            "gpu_launches": args.steps * (5 * LAYERS + 1 + (4 * LAYERS + 1 if tokens <= kernels.GEMV_MAX_ROWS else 0)),
+            "gpu_launches": args.steps * _step_launches(tokens),
             "gpu_launches_attention_per_step": LAYERS,
             "logits_finite": bool(torch.isfinite(logits).all().item()),
             "clocks": clocks.summary(),

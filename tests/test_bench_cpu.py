@@ -76,3 +76,14 @@ def test_clock_samples_are_kept_only_inside_the_timed_window(monkeypatch) -> Non
     samples, max_mhz, error = sent[0]
     assert error is None and max_mhz == 1965.0
     assert samples and all(mhz == 1965.0 and bits == 0x4 for mhz, bits in samples)
+
+
+def test_decoder_launch_count_follows_the_projection_routing() -> None:
+    """The decoder and prefill legs' `gpu_launches` per step: 256 rows (library GEMMs) 5 per
+    layer + the final norm; 32 rows adds the tcgen05 linear layer's 4 per layer
+    + the LM head and a Q/K/V split-sum per layer (the launch list of a 32-row
+    step, two steps of 448 launches of which 4 are ATen, gives 222); one row
+    adds the matrix-vector kernel's 4 per layer + the LM head."""
+    assert bench._step_launches(256) == 22 * 5 + 1
+    assert bench._step_launches(32) == 222
+    assert bench._step_launches(1) == 22 * 5 + 1 + 22 * 4 + 1
