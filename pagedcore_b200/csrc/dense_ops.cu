@@ -127,6 +127,96 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(
     }
 }
 
+// The same operation for rows of up to 2048 values, one warp per row and
+// two rows per CTA, bit for bit add_rms_norm_kernel's result: lane l holds
+// the chunks of that kernel's threads l, 32 + l, ..., 224 + l (one chunk
+// each at this width), sums each one's squares in the same order, reduces
+// each group of 32 across the lanes with the same butterfly as that kernel's
+// warps, and adds the eight group sums in order.  A lane has all of its
+// loads (hidden, delta and weight) in flight at once, and a prompt's rows fit
+// one wave, where one CTA of 256 threads per row (three resident per SM)
+// waits on its loads, its block-wide reduction and then its weight row, in
+// several waves.  Used from kRowKernelMinRows rows: measured on B200 at 2047
+// rows a prefill step took 5.27 ms with it against 5.38-5.43, while at 256
+// rows (one wave of the CTA kernel) a form with eight rows per CTA made the
+// decoder step slower (2.264 against 2.217-2.223 ms).
+constexpr int kRowWarps = 2;                      // rows per CTA
+constexpr int kRowKernelMinRows = 512;
+constexpr int kRowGroups = kNormThreads / 32;     // add_rms_norm_kernel's warps
+constexpr int kRowMaxDim = kRowGroups * 32 * kChunk;  // 2048
+
+__global__ void __launch_bounds__(kRowWarps * 32) add_rms_norm_rows_kernel(
+    __half *__restrict__ hidden, const __half *__restrict__ delta, const __half *__restrict__ weight,
+    __half *__restrict__ out, int rows, int dim, float eps) {
+    pkv::pdl_launch_dependents();
+    pkv::pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int64_t base = static_cast<int64_t>(row) * dim;
+    const int chunks = dim / kChunk;
+    uint4 raw[kRowGroups], draw[kRowGroups], wraw[kRowGroups];
+#pragma unroll
+    for (int g = 0; g < kRowGroups; ++g) {
+        const int c = g * 32 + lane;
+        if (c < chunks) {
+            raw[g] = *reinterpret_cast<const uint4 *>(hidden + base + c * kChunk);
+            if (delta != nullptr) draw[g] = *reinterpret_cast<const uint4 *>(delta + base + c * kChunk);
+            wraw[g] = *reinterpret_cast<const uint4 *>(weight + c * kChunk);
+        }
+    }
+    float group[kRowGroups];
+#pragma unroll
+    for (int g = 0; g < kRowGroups; ++g) {
+        const int c = g * 32 + lane;
+        float sum = 0.f;
+        if (c < chunks) {
+            if (delta != nullptr) {
+                const __half *h = reinterpret_cast<const __half *>(&raw[g]);
+                const __half *d = reinterpret_cast<const __half *>(&draw[g]);
+                uint4 sum_raw;
+                __half *s = reinterpret_cast<__half *>(&sum_raw);
+#pragma unroll
+                for (int i = 0; i < kChunk; ++i) s[i] = __float2half_rn(h2f(h[i]) + h2f(d[i]));
+                *reinterpret_cast<uint4 *>(hidden + base + c * kChunk) = sum_raw;
+                raw[g] = sum_raw;
+            }
+            const __half *h = reinterpret_cast<const __half *>(&raw[g]);
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                const float v = h2f(h[i]);
+                sum += v * v;
+            }
+        }
+        group[g] = sum;
+    }
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+#pragma unroll
+        for (int g = 0; g < kRowGroups; ++g) group[g] += __shfl_xor_sync(0xffffffffu, group[g], offset);
+    }
+    float total = 0.f;
+#pragma unroll
+    for (int g = 0; g < kRowGroups; ++g) total += group[g];
+    const float inv = rsqrtf(total / static_cast<float>(dim) + eps);
+#pragma unroll
+    for (int g = 0; g < kRowGroups; ++g) {
+        const int c = g * 32 + lane;
+        if (c < chunks) {
+            const __half *h = reinterpret_cast<const __half *>(&raw[g]);
+            const __half *w = reinterpret_cast<const __half *>(&wraw[g]);
+            uint4 oraw;
+            __half *o = reinterpret_cast<__half *>(&oraw);
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                const __half y = __float2half_rn(h2f(h[i]) * inv);
+                o[i] = __float2half_rn(h2f(w[i]) * h2f(y));
+            }
+            *reinterpret_cast<uint4 *>(out + base + c * kChunk) = oraw;
+        }
+    }
+}
+
 __device__ __forceinline__ __half silu_times(__half gate, __half up) {
     const float g = h2f(gate);
     const __half silu = __float2half_rn(g / (1.0f + expf(-g)));
@@ -193,10 +283,16 @@ extern "C" int pkv_add_rms_norm(void *hidden, const void *delta, const void *wei
         return pkv::fail(PKV_VALUE_ERROR, "rms norm: tensors must be 16-byte aligned");
     }
     if (rows == 0) return PKV_OK;
-    const cudaError_t err = pkv::launch_pdl(
-        add_rms_norm_kernel, dim3(rows), dim3(kNormThreads), static_cast<cudaStream_t>(stream),
-        static_cast<__half *>(hidden), static_cast<const __half *>(delta), static_cast<const float *>(nullptr), 0,
-        static_cast<int64_t>(0), static_cast<const __half *>(weight), static_cast<__half *>(out), dim, eps);
+    const cudaError_t err =
+        dim <= kRowMaxDim && rows >= kRowKernelMinRows
+            ? pkv::launch_pdl(add_rms_norm_rows_kernel, dim3((rows + kRowWarps - 1) / kRowWarps), dim3(kRowWarps * 32),
+                              static_cast<cudaStream_t>(stream), static_cast<__half *>(hidden),
+                              static_cast<const __half *>(delta), static_cast<const __half *>(weight),
+                              static_cast<__half *>(out), static_cast<int>(rows), static_cast<int>(dim), eps)
+            : pkv::launch_pdl(add_rms_norm_kernel, dim3(rows), dim3(kNormThreads), static_cast<cudaStream_t>(stream),
+                              static_cast<__half *>(hidden), static_cast<const __half *>(delta),
+                              static_cast<const float *>(nullptr), 0, static_cast<int64_t>(0),
+                              static_cast<const __half *>(weight), static_cast<__half *>(out), dim, eps);
     if (err != cudaSuccess) return pkv::fail(PKV_CUDA_ERROR, std::string("rms norm launch failed: ") + cudaGetErrorString(err));
     return PKV_OK;
 }

@@ -114,3 +114,27 @@ def test_gemv_takes_strided_rows_and_leaves_other_shapes_to_the_library() -> Non
     assert torch.equal(kernels.linear(many, weight), torch.nn.functional.linear(many, weight))
     with pytest.raises(ValueError, match="1 to 8 rows"):
         gemv(many, weight, torch.empty(9, 96, dtype=torch.float16, device=device))
+
+
+@pytest.mark.parametrize("rows", [512, 2047])
+def test_add_rms_norm_of_a_prompt_equals_the_small_batch_kernel_bit_for_bit(rows) -> None:
+    """From 512 rows the norm runs one warp per row; it sums the squares in the
+    order of the kernel used below 512 rows, so the same rows normalised in
+    batches of 256 give the same bits (the residual add in place, and out)."""
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(rows + 1)
+    hidden = torch.randn(rows, 2048, dtype=torch.float16, device=device, generator=generator)
+    delta = torch.randn(rows, 2048, dtype=torch.float16, device=device, generator=generator)
+    weight = (1 + 0.1 * torch.randn(2048, device=device, generator=generator)).half()
+    for with_delta in (True, False):
+        whole, parts = hidden.clone(), hidden.clone()
+        out_whole, out_parts = torch.empty_like(hidden), torch.empty_like(hidden)
+        kernels.add_rms_norm(whole, delta if with_delta else None, weight, out_whole)
+        for begin in range(0, rows, 256):
+            end = min(begin + 256, rows)
+            kernels.add_rms_norm(parts[begin:end], delta[begin:end] if with_delta else None, weight,
+                                 out_parts[begin:end])
+        assert torch.equal(whole, parts) and torch.equal(out_whole, out_parts)
+        if with_delta:
+            assert torch.equal(whole, hidden + delta)
+        ulp_close(out_whole, rms_norm(whole, weight), ulps=2)
