@@ -60,6 +60,23 @@ def test_silu_mul_matches_the_eager_swiglu_product(rows, inter) -> None:
     ulp_close(kernels.silu_mul(gate_up), F.silu(gate) * up)
 
 
+def test_silu_mul_pairs_equal_the_one_value_path_bit_for_bit() -> None:
+    """The 16-byte path multiplies two values at once in FP16 (the FP32 product
+    of two FP16 values is exact, so its FP16 rounding is the FP16 multiply);
+    the one-value path, taken for operands off 16-byte alignment, rounds the
+    FP32 product.  Both must give the same bits."""
+    device = cuda_device()
+    generator = torch.Generator(device=device).manual_seed(5)
+    rows, inter = 300, 5632
+    buffer = torch.empty(rows * 2 * inter + 1, dtype=torch.float16, device=device)
+    buffer[1:] = 3 * torch.randn(rows * 2 * inter, dtype=torch.float16, device=device, generator=generator)
+    unaligned = buffer[1:].view(rows, 2 * inter)
+    assert unaligned.data_ptr() % 16
+    aligned = unaligned.clone()
+    assert aligned.data_ptr() % 16 == 0
+    assert torch.equal(kernels.silu_mul(aligned), kernels.silu_mul(unaligned))
+
+
 def test_fused_ops_reject_bad_shapes() -> None:
     device = cuda_device()
     hidden = torch.zeros(2, 2048, dtype=torch.float16, device=device)
